@@ -1,0 +1,76 @@
+"""ctypes binding of libaffon_b200.so (include/affon_b200.h).
+
+The shared library is built in-tree by affon_b200/csrc/Makefile.  Loading it
+never falls back to anything: a missing or unloadable library raises.
+"""
+import ctypes
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libaffon_b200.so"
+HEADER = HERE.parent / "include" / "affon_b200.h"
+
+OK, INVALID_SHAPE, UNSUPPORTED, CUDA_ERROR, TIMEOUT, GUARD_MISMATCH, POLICY_REJECTED, INVALID_ARG, INVALID_DTYPE = range(9)
+F32, BF16, U32 = 0, 1, 2
+POLICY = {"backend_equivalent": 0, "exact_only": 1, "approximate": 2}
+NUMERICS = {0: "exact", 1: "reassociated", 2: "approximate"}
+
+c_i64, c_i32, c_u32, c_vp, c_sz = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t
+
+
+class View(ctypes.Structure):
+    _fields_ = [("rows", c_i64), ("cols", c_i64), ("row_stride", c_i64), ("col_stride", c_i64), ("byte_offset", c_i64)]
+
+
+class QmmDesc(ctypes.Structure):
+    _fields_ = [("struct_size", c_u32), ("bits", c_i32), ("group_size", c_i64), ("x_dtype", c_i32),
+                ("param_dtype", c_i32), ("y_dtype", c_i32), ("numerical_policy", c_i32), ("dense_inputs", c_i32),
+                ("reserved", c_i32), ("x", View), ("w", View), ("s", View), ("b", View), ("y", View)]
+
+
+class Selection(ctypes.Structure):
+    _fields_ = [("implementation_id", ctypes.c_char * 64), ("implementation_version", c_i32),
+                ("numerical_class", c_i32), ("splits", c_i32), ("reserved", c_i32), ("reason", ctypes.c_char * 256)]
+
+
+# Every function include/affon_b200.h declares, with its ctypes signature.
+SIGNATURES = {
+    "affon_b200_abi_version": ([], c_i32),
+    "affon_b200_last_error": ([], ctypes.c_char_p),
+    "affon_b200_ctx_create": ([c_i32, c_vp, ctypes.POINTER(c_vp)], c_i32),
+    "affon_b200_ctx_destroy": ([c_vp], c_i32),
+    "affon_b200_ctx_set_stream": ([c_vp, c_vp], c_i32),
+    "affon_b200_ctx_device": ([c_vp], c_i32),
+    "affon_b200_ctx_reserve_workspace": ([c_vp, c_sz], c_i32),
+    "affon_b200_validate": ([ctypes.POINTER(QmmDesc)], c_i32),
+    "affon_b200_select": ([ctypes.POINTER(QmmDesc), ctypes.POINTER(Selection)], c_i32),
+    "affon_b200_qmm": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_qmm_explain": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp,
+                                ctypes.POINTER(Selection)], c_i32),
+    "affon_b200_qmm_host": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_compute_core_run_quantized_matmul_f32": ([c_vp, c_sz, c_vp, c_sz, c_vp, c_sz, c_vp, c_sz, c_vp, c_sz,
+                                                          c_sz, c_sz, c_sz, c_sz, c_sz], c_i32),
+    "affon_b200_launch_count": ([], ctypes.c_uint64),
+}
+
+_lib = None
+
+
+def lib():
+    """Load the native library (raises if it is missing: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is not built; run `make -C affon_b200/csrc` (or __graft_entry__.build())")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def last_error():
+    msg = lib().affon_b200_last_error()
+    return msg.decode() if msg else ""

@@ -1,0 +1,446 @@
+// C ABI of the affon_b200 library: contexts, validation, physical selection
+// and dispatch for quantized_matmul.  See include/affon_b200.h.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "../../include/affon_b200.h"
+#include "internal.h"
+
+struct affon_b200_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    void *workspace = nullptr;
+    size_t workspace_bytes = 0;
+    // Staging buffers of the host-buffer entry points (grown on demand).
+    void *stage[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t stage_bytes[5] = {0, 0, 0, 0, 0};
+};
+
+namespace afb {
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+}  // namespace afb
+
+namespace {
+
+thread_local std::string t_error;
+
+int fail(int status, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(AFFON_B200_CUDA_ERROR, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+constexpr size_t kDefaultWorkspace = size_t(32) << 20;
+
+// Makes ctx->device current for the scope of one call.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int env_device() {
+    const char *v = getenv("AFFON_CUDA_DEVICE");
+    if (!v || !*v) return 0;
+    char *end = nullptr;
+    long d = strtol(v, &end, 10);
+    if (*end || d < 0) return -1;
+    return static_cast<int>(d);
+}
+
+bool is_float_dtype(int d) { return d == AFFON_B200_F32 || d == AFFON_B200_BF16; }
+size_t dtype_size(int d) { return d == AFFON_B200_BF16 ? 2 : 4; }
+
+bool view_dense(const affon_b200_view &v) {
+    return v.byte_offset == 0 && v.col_stride == 1 && v.row_stride == v.cols;
+}
+
+// Largest element index a view touches, plus one (strides are non-negative).
+int64_t view_extent(const affon_b200_view &v) {
+    return (v.rows - 1) * v.row_stride + (v.cols - 1) * v.col_stride + 1;
+}
+
+int validate_desc(const affon_b200_qmm_desc *d) {
+    if (!d) return fail(AFFON_B200_INVALID_ARG, "quantized_matmul: null descriptor");
+    if (d->struct_size != sizeof(affon_b200_qmm_desc))
+        return fail(AFFON_B200_INVALID_ARG, "quantized_matmul: descriptor struct_size %u, expected %zu", d->struct_size,
+                    sizeof(affon_b200_qmm_desc));
+    // program.ts:483-484
+    if (d->bits != 2 && d->bits != 4 && d->bits != 8)
+        return fail(AFFON_B200_INVALID_SHAPE, "quantized_matmul bits must be 2, 4, or 8");
+    if (d->group_size <= 0) return fail(AFFON_B200_INVALID_SHAPE, "quantized_matmul group_size must be a positive integer");
+    // program.ts:486-487
+    if (!is_float_dtype(d->x_dtype) || !is_float_dtype(d->param_dtype))
+        return fail(AFFON_B200_INVALID_DTYPE,
+                    "quantized_matmul requires f32/bf16 input, u32 weights, and matching f32/bf16 scales and biases");
+    if (!is_float_dtype(d->y_dtype)) return fail(AFFON_B200_INVALID_DTYPE, "quantized_matmul result dtype must be f32 or bf16");
+    const affon_b200_view *vs[5] = {&d->x, &d->w, &d->s, &d->b, &d->y};
+    for (const affon_b200_view *v : vs) {
+        if (v->rows < 0 || v->cols < 0 || v->row_stride < 0 || v->col_stride < 0 || v->byte_offset < 0)
+            return fail(AFFON_B200_INVALID_ARG, "quantized_matmul: negative view extent, stride or offset");
+    }
+    // program.ts:488-492
+    const int64_t rows = d->x.rows, inner = d->x.cols, outputs = d->w.rows;
+    const int64_t per_word = 32 / d->bits;
+    if (!rows || !inner || !outputs || inner % per_word || inner % d->group_size || d->w.cols != inner / per_word ||
+        d->s.rows != outputs || d->s.cols != inner / d->group_size || d->b.rows != outputs ||
+        d->b.cols != inner / d->group_size)
+        return fail(AFFON_B200_INVALID_SHAPE, "quantized_matmul packed or group dimensions do not match input features");
+    // Result spec f32 [rows, outputs] (program.ts:494).
+    if (d->y.rows != rows || d->y.cols != outputs)
+        return fail(AFFON_B200_INVALID_SHAPE, "quantized_matmul result view must be [%lld, %lld]", (long long)rows,
+                    (long long)outputs);
+    if (d->y.col_stride != 1 || d->y.row_stride < outputs)
+        return fail(AFFON_B200_UNSUPPORTED, "quantized_matmul result view must have dense rows");
+    if (rows > (int64_t(1) << 40) / inner || outputs > (int64_t(1) << 40) / inner || rows > (int64_t(1) << 40) / outputs)
+        return fail(AFFON_B200_INVALID_SHAPE, "quantized_matmul dimensions overflow");
+    if (d->dense_inputs) {
+        // optimization-and-profiling.md:143-151: incompatible views fail with GuardMismatch.
+        if (!view_dense(d->x) || !view_dense(d->w) || !view_dense(d->s) || !view_dense(d->b))
+            return fail(AFFON_B200_GUARD_MISMATCH, "GuardMismatch: denseInputs requires dense, zero-offset inputs");
+    }
+    if (d->numerical_policy < 0 || d->numerical_policy > 2)
+        return fail(AFFON_B200_INVALID_ARG, "quantized_matmul: unknown numerical policy %d", d->numerical_policy);
+    return AFFON_B200_OK;
+}
+
+afb::QmmArgs make_args(const affon_b200_qmm_desc *d, const void *x, const void *w, const void *s, const void *b,
+                       void *y) {
+    afb::QmmArgs a{};
+    auto view = [](const void *base, const affon_b200_view &v) {
+        return afb::View{static_cast<const char *>(base) + v.byte_offset, v.row_stride, v.col_stride};
+    };
+    a.x = view(x, d->x);
+    a.w = view(w, d->w);
+    a.s = view(s, d->s);
+    a.b = view(b, d->b);
+    a.y = static_cast<char *>(y) + d->y.byte_offset;
+    a.ldy = d->y.row_stride;
+    a.M = d->x.rows;
+    a.N = d->w.rows;
+    a.K = d->x.cols;
+    a.group = d->group_size;
+    a.bits = d->bits;
+    a.x_bf16 = d->x_dtype == AFFON_B200_BF16;
+    a.p_bf16 = d->param_dtype == AFFON_B200_BF16;
+    a.y_bf16 = d->y_dtype == AFFON_B200_BF16;
+    return a;
+}
+
+enum Impl { IMPL_GENERIC = 0, IMPL_QMV = 1, IMPL_QMM_TC = 2 };
+
+struct Choice {
+    Impl impl;
+    afb::QmvPlan plan;
+    int passes;  // qmv passes over 16-row slices of M
+};
+
+int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms, size_t workspace,
+                affon_b200_selection *sel, Choice *out) {
+    // quantized-inference.md:175-177: quantized candidates are `reassociated`;
+    // exact_only rejects them.
+    if (d->numerical_policy == AFFON_B200_POLICY_EXACT_ONLY)
+        return fail(AFFON_B200_POLICY_REJECTED,
+                    "numericalPolicy exact_only rejects cuda_quantized_matmul (numerical class reassociated)");
+    Choice c{IMPL_GENERIC, {}, 1};
+    char reason[256];
+    const char *why_qmv = "";
+    afb::QmmArgs probe = a;
+    probe.M = a.M < 16 ? a.M : 16;
+    const bool qmv_ok = afb::qmv_supported(probe, &why_qmv);
+    const char *why_tc = "";
+    const bool tc_ok = afb::qmm_tc_supported(a, &why_tc);
+    if (qmv_ok && a.M <= 16) {
+        c.impl = IMPL_QMV;
+        c.plan = afb::qmv_plan(a, num_sms, workspace);
+        snprintf(reason, sizeof reason, "M=%lld <= 16: decode qmv, split-K %d, %d CTAs per split", (long long)a.M,
+                 c.plan.splits, c.plan.grid_n);
+    } else if (tc_ok && (d->numerical_policy == AFFON_B200_POLICY_APPROXIMATE || a.y_bf16)) {
+        c.impl = IMPL_QMM_TC;
+        snprintf(reason, sizeof reason, "M=%lld >= 64: tcgen05 qmm with bf16-rounded decoded weights", (long long)a.M);
+    } else if (qmv_ok && a.M <= 64) {
+        c.impl = IMPL_QMV;
+        c.passes = static_cast<int>((a.M + 15) / 16);
+        c.plan = afb::qmv_plan(probe, num_sms, workspace);
+        snprintf(reason, sizeof reason, "16 < M=%lld <= 64: %d qmv passes over 16-row slices", (long long)a.M,
+                 c.passes);
+    } else {
+        snprintf(reason, sizeof reason, "generic strided kernel (%s%s%s)", why_qmv, tc_ok ? "" : "; ",
+                 tc_ok ? "" : why_tc);
+    }
+    if (sel) {
+        memset(sel, 0, sizeof *sel);
+        if (c.impl == IMPL_QMV)
+            snprintf(sel->implementation_id, sizeof sel->implementation_id, "cuda_quantized_matmul.sm100_qmv_b%d_g64",
+                     d->bits);
+        else if (c.impl == IMPL_QMM_TC)
+            snprintf(sel->implementation_id, sizeof sel->implementation_id,
+                     "cuda_quantized_matmul.sm100_qmm_tcgen05_b%d_g64", d->bits);
+        else
+            snprintf(sel->implementation_id, sizeof sel->implementation_id, "cuda_quantized_matmul.sm100_generic");
+        sel->implementation_version = 1;
+        sel->numerical_class = c.impl == IMPL_QMM_TC ? AFFON_B200_APPROXIMATE : AFFON_B200_REASSOCIATED;
+        sel->splits = c.impl == IMPL_QMV ? c.plan.splits : 1;
+        snprintf(sel->reason, sizeof sel->reason, "%s", reason);
+    }
+    *out = c;
+    return AFFON_B200_OK;
+}
+
+int launch(affon_b200_ctx *ctx, const afb::QmmArgs &a, const Choice &c) {
+    cudaError_t e = cudaSuccess;
+    switch (c.impl) {
+    case IMPL_QMV: {
+        for (int pass = 0; pass < c.passes && e == cudaSuccess; ++pass) {
+            afb::QmmArgs slice = a;
+            const int64_t m0 = int64_t(pass) * 16;
+            slice.M = (a.M - m0) < 16 ? (a.M - m0) : 16;
+            slice.x.ptr = static_cast<const char *>(a.x.ptr) + m0 * a.x.row_stride * 2;
+            slice.y = static_cast<char *>(a.y) + m0 * a.ldy * (a.y_bf16 ? 2 : 4);
+            afb::QmvPlan plan = c.passes == 1 ? c.plan : afb::qmv_plan(slice, ctx->num_sms, ctx->workspace_bytes);
+            if (afb::qmv_workspace_bytes(slice, plan) > ctx->workspace_bytes)
+                return fail(AFFON_B200_CUDA_ERROR, "qmv plan exceeds the context workspace");
+            e = afb::launch_qmv(slice, plan, ctx->workspace, ctx->stream);
+        }
+        break;
+    }
+    case IMPL_QMM_TC:
+        e = afb::launch_qmm_tc(a, ctx->stream);
+        break;
+    default:
+        e = afb::launch_qmm_generic(a, ctx->stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul launch");
+    return AFFON_B200_OK;
+}
+
+int grow(void **buf, size_t *have, size_t need) {
+    if (*have >= need) return AFFON_B200_OK;
+    if (*buf) cudaFree(*buf);
+    *buf = nullptr;
+    *have = 0;
+    size_t want = need < 256 ? 256 : need;
+    cudaError_t e = cudaMalloc(buf, want);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    *have = want;
+    return AFFON_B200_OK;
+}
+
+thread_local affon_b200_ctx *t_default_ctx = nullptr;
+
+}  // namespace
+
+extern "C" {
+
+int affon_b200_abi_version(void) { return AFFON_B200_ABI_VERSION; }
+
+const char *affon_b200_last_error(void) { return t_error.c_str(); }
+
+uint64_t affon_b200_launch_count(void) { return afb::g_launches.load(); }
+
+int affon_b200_ctx_create(int device_ordinal, void *cuda_stream, affon_b200_ctx **out) {
+    if (!out) return fail(AFFON_B200_INVALID_ARG, "ctx_create: null output pointer");
+    *out = nullptr;
+    int dev = device_ordinal >= 0 ? device_ordinal : env_device();
+    if (dev < 0) return fail(AFFON_B200_INVALID_ARG, "AFFON_CUDA_DEVICE must be a non-negative integer");
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) return fail(AFFON_B200_UNSUPPORTED, "backend unavailable: no CUDA device");
+    if (dev >= count) return fail(AFFON_B200_INVALID_ARG, "CUDA device %d out of range (%d devices)", dev, count);
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(AFFON_B200_UNSUPPORTED, "backend unavailable: affon_b200 requires sm_100 (found sm_%d%d)", prop.major,
+                    prop.minor);
+    DeviceGuard guard(dev);
+    if (!guard.ok) return fail(AFFON_B200_CUDA_ERROR, "cudaSetDevice(%d) failed", dev);
+    affon_b200_ctx *c = new affon_b200_ctx;
+    c->device = dev;
+    c->stream = static_cast<cudaStream_t>(cuda_stream);
+    c->num_sms = prop.multiProcessorCount;
+    int rc = affon_b200_ctx_reserve_workspace(c, kDefaultWorkspace);
+    if (rc) {
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return AFFON_B200_OK;
+}
+
+int affon_b200_ctx_destroy(affon_b200_ctx *ctx) {
+    if (!ctx) return AFFON_B200_OK;
+    DeviceGuard guard(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    else cudaDeviceSynchronize();
+    if (ctx->workspace) cudaFree(ctx->workspace);
+    for (void *p : ctx->stage)
+        if (p) cudaFree(p);
+    if (t_default_ctx == ctx) t_default_ctx = nullptr;
+    delete ctx;
+    return AFFON_B200_OK;
+}
+
+int affon_b200_ctx_set_stream(affon_b200_ctx *ctx, void *cuda_stream) {
+    if (!ctx) return fail(AFFON_B200_INVALID_ARG, "null context");
+    ctx->stream = static_cast<cudaStream_t>(cuda_stream);
+    return AFFON_B200_OK;
+}
+
+int affon_b200_ctx_device(const affon_b200_ctx *ctx) { return ctx ? ctx->device : -1; }
+
+int affon_b200_ctx_reserve_workspace(affon_b200_ctx *ctx, size_t bytes) {
+    if (!ctx) return fail(AFFON_B200_INVALID_ARG, "null context");
+    if (bytes <= ctx->workspace_bytes) return AFFON_B200_OK;
+    DeviceGuard guard(ctx->device);
+    // The old workspace may still be in use by queued launches.
+    if (ctx->workspace) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(ctx->workspace);
+        ctx->workspace = nullptr;
+        ctx->workspace_bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&ctx->workspace, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "workspace cudaMalloc");
+    // Split-K arrival counters must start at zero; launches leave them zero.
+    if ((e = cudaMemset(ctx->workspace, 0, bytes)) != cudaSuccess) return cuda_fail(e, "workspace cudaMemset");
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "workspace init");
+    ctx->workspace_bytes = bytes;
+    return AFFON_B200_OK;
+}
+
+int affon_b200_validate(const affon_b200_qmm_desc *desc) {
+    t_error.clear();
+    return validate_desc(desc);
+}
+
+int affon_b200_select(const affon_b200_qmm_desc *desc, affon_b200_selection *out) {
+    t_error.clear();
+    int rc = validate_desc(desc);
+    if (rc) return rc;
+    // Selection needs only shapes, dtypes and alignment; use placeholder
+    // 256-byte-aligned device addresses for the alignment rules.
+    char *fake = reinterpret_cast<char *>(uintptr_t(1) << 40);
+    afb::QmmArgs a = make_args(desc, fake, fake, fake, fake, fake);
+    Choice c;
+    return select_impl(desc, a, 148, kDefaultWorkspace, out, &c);
+}
+
+int affon_b200_qmm_explain(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
+                           const void *s, const void *b, void *y, affon_b200_selection *sel) {
+    t_error.clear();
+    if (!ctx) return fail(AFFON_B200_INVALID_ARG, "null context");
+    int rc = validate_desc(desc);
+    if (rc) return rc;
+    if (!x || !w || !s || !b || !y) return fail(AFFON_B200_INVALID_ARG, "quantized_matmul: null buffer");
+    afb::QmmArgs a = make_args(desc, x, w, s, b, y);
+    Choice c;
+    rc = select_impl(desc, a, ctx->num_sms, ctx->workspace_bytes, sel, &c);
+    if (rc) return rc;
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(AFFON_B200_CUDA_ERROR, "cudaSetDevice(%d) failed", ctx->device);
+    return launch(ctx, a, c);
+}
+
+int affon_b200_qmm(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
+                   const void *s, const void *b, void *y) {
+    return affon_b200_qmm_explain(ctx, desc, x, w, s, b, y, nullptr);
+}
+
+int affon_b200_qmm_host(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
+                        const void *s, const void *b, void *y) {
+    t_error.clear();
+    if (!ctx) return fail(AFFON_B200_INVALID_ARG, "null context");
+    int rc = validate_desc(desc);
+    if (rc) return rc;
+    if (!x || !w || !s || !b || !y) return fail(AFFON_B200_INVALID_ARG, "quantized_matmul: null buffer");
+    DeviceGuard guard(ctx->device);
+    if (!guard.ok) return fail(AFFON_B200_CUDA_ERROR, "cudaSetDevice(%d) failed", ctx->device);
+    const void *host[4] = {x, w, s, b};
+    const affon_b200_view *views[4] = {&desc->x, &desc->w, &desc->s, &desc->b};
+    const size_t esz[4] = {dtype_size(desc->x_dtype), 4, dtype_size(desc->param_dtype), dtype_size(desc->param_dtype)};
+    size_t bytes[5];
+    for (int i = 0; i < 4; ++i) bytes[i] = views[i]->byte_offset + size_t(view_extent(*views[i])) * esz[i];
+    const size_t ysz = dtype_size(desc->y_dtype);
+    bytes[4] = desc->y.byte_offset + size_t(view_extent(desc->y)) * ysz;
+    for (int i = 0; i < 5; ++i)
+        if ((rc = grow(&ctx->stage[i], &ctx->stage_bytes[i], bytes[i]))) return rc;
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 4 && e == cudaSuccess; ++i)
+        e = cudaMemcpyAsync(ctx->stage[i], host[i], bytes[i], cudaMemcpyHostToDevice, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "host-to-device copy");
+    afb::QmmArgs a = make_args(desc, ctx->stage[0], ctx->stage[1], ctx->stage[2], ctx->stage[3], ctx->stage[4]);
+    Choice c;
+    if ((rc = select_impl(desc, a, ctx->num_sms, ctx->workspace_bytes, nullptr, &c))) return rc;
+    if ((rc = launch(ctx, a, c))) return rc;
+    // Copy back only the rows of y (dense rows of N elements at row stride ldy).
+    const size_t row_bytes = size_t(desc->y.cols) * ysz;
+    e = cudaMemcpy2DAsync(static_cast<char *>(y) + desc->y.byte_offset, size_t(desc->y.row_stride) * ysz,
+                          static_cast<char *>(ctx->stage[4]) + desc->y.byte_offset, size_t(desc->y.row_stride) * ysz,
+                          row_bytes, size_t(desc->y.rows), cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "device-to-host copy");
+    if ((e = cudaStreamSynchronize(ctx->stream)) != cudaSuccess) return cuda_fail(e, "stream synchronize");
+    return AFFON_B200_OK;
+}
+
+int affon_b200_compute_core_run_quantized_matmul_f32(const float *activation, size_t activation_count,
+                                                     const uint32_t *weights, size_t weight_count, const float *scales,
+                                                     size_t scale_count, const float *biases, size_t bias_count,
+                                                     float *output, size_t output_count, size_t rows, size_t depth,
+                                                     size_t columns, size_t bits, size_t group_size) {
+    t_error.clear();
+    // compute_core_cyna.zig:1013-1023 shape rules.
+    if (rows == 0 || depth == 0 || columns == 0 || group_size == 0 || (bits != 2 && bits != 4 && bits != 8))
+        return fail(AFFON_B200_INVALID_SHAPE, "InvalidShape");
+    const size_t per_word = 32 / bits;
+    if (depth % per_word || depth % group_size) return fail(AFFON_B200_INVALID_SHAPE, "InvalidShape");
+    const size_t lim = size_t(1) << 40;
+    if (rows > lim / depth || columns > lim / depth || rows > lim / columns)
+        return fail(AFFON_B200_INVALID_SHAPE, "InvalidShape");
+    if (activation_count != rows * depth || weight_count != columns * (depth / per_word) ||
+        scale_count != columns * (depth / group_size) || bias_count != columns * (depth / group_size) ||
+        output_count != rows * columns)
+        return fail(AFFON_B200_INVALID_SHAPE, "InvalidShape");
+    if (!activation || !weights || !scales || !biases || !output) return fail(AFFON_B200_INVALID_ARG, "null buffer");
+    if (!t_default_ctx) {
+        int rc = affon_b200_ctx_create(-1, nullptr, &t_default_ctx);
+        if (rc) return rc;
+    }
+    affon_b200_qmm_desc d{};
+    d.struct_size = sizeof d;
+    d.bits = int32_t(bits);
+    d.group_size = int64_t(group_size);
+    d.x_dtype = d.param_dtype = d.y_dtype = AFFON_B200_F32;
+    d.numerical_policy = AFFON_B200_POLICY_BACKEND_EQUIVALENT;
+    const int64_t M = int64_t(rows), N = int64_t(columns), K = int64_t(depth);
+    d.x = {M, K, K, 1, 0};
+    d.w = {N, K / int64_t(per_word), K / int64_t(per_word), 1, 0};
+    d.s = d.b = {N, K / int64_t(group_size), K / int64_t(group_size), 1, 0};
+    d.y = {M, N, N, 1, 0};
+    return affon_b200_qmm_host(t_default_ctx, &d, activation, weights, scales, biases, output);
+}
+
+}  // extern "C"

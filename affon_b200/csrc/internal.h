@@ -1,0 +1,47 @@
+// Internal launch interfaces shared by the C-ABI layer and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace afb {
+
+// A resolved operand: device base already offset by the view's byte offset.
+struct View {
+    const void *ptr;
+    int64_t row_stride;
+    int64_t col_stride;
+};
+
+struct QmmArgs {
+    View x, w, s, b;
+    void *y;
+    int64_t ldy;
+    int64_t M, N, K, group;
+    int bits;
+    int x_bf16, p_bf16, y_bf16;
+};
+
+// Generic strided kernel: any bits / group / dtype / view; one thread per
+// output element, same operation order as the CPU oracle.
+cudaError_t launch_qmm_generic(const QmmArgs &a, cudaStream_t stream);
+
+// Decode qmv for M <= 16, bits in {4, 8}, group 64, bf16 x/s/b, dense rows.
+struct QmvPlan {
+    int splits;            // split-K factor (>= 1)
+    int blocks_per_split;  // pipeline blocks (4 groups each) per split
+    int grid_n;            // CTAs along N per split
+    int smem_bytes;
+};
+bool qmv_supported(const QmmArgs &a, const char **why);
+QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes);
+size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p);
+cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &p, void *workspace, cudaStream_t stream);
+
+// Prefill qmm on tcgen05 tensor cores (M >= 64), bf16 x/s/b, 4/8-bit, group 64.
+bool qmm_tc_supported(const QmmArgs &a, const char **why);
+cudaError_t launch_qmm_tc(const QmmArgs &a, cudaStream_t stream);
+
+void count_launch(uint64_t n = 1);
+
+}  // namespace afb

@@ -1,0 +1,170 @@
+/*
+ * affon_b200 — C ABI of the sm_100a kernel library for Affon's affine
+ * group-quantized matmul (`affon:ops.quantized_matmul`).
+ *
+ * This is the boundary the reference's CUDA device backend would bind.  In the
+ * reference the operation reaches its backend through
+ *   src/js/ops.ts:69-79 (public op) -> src/js/compute/program.ts:481-495
+ *   (validation, f32 [M,N] result spec) -> src/js/compute/native.zig:731-746,851
+ *   (lowering to compute.OpTag.quantized_matmul with {bits, group_size}) ->
+ *   the compute core's physical selection of `cuda_quantized_matmul`
+ *   (docs/core/quantized-inference.md:175-181) -> the CUDA backend launch.
+ * The only in-tree C-ABI form of the operation is the Cyna adapter
+ * `compute_core_run_quantized_matmul_f32` (src/support/compute_core_cyna.zig:29-45);
+ * its status codes (0 ok, 1 invalid shape) and its rule that the output is left
+ * untouched on error are kept here.
+ *
+ * Plain pointers and sizes only.  Device pointers are caller-owned; the
+ * library never allocates outputs.  Launches are asynchronous on the stream of
+ * the context; validation happens on the host before any launch.
+ */
+#ifndef AFFON_B200_H
+#define AFFON_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AFFON_B200_ABI_VERSION 1
+
+/* Status codes.  0/1 follow compute_core_cyna.zig:1000-1032 (0 ok,
+ * 1 InvalidShape); the rest name the reference's other failure classes. */
+typedef enum affon_b200_status {
+    AFFON_B200_OK = 0,
+    AFFON_B200_INVALID_SHAPE = 1,   /* program.ts:484-493 shape/option rules */
+    AFFON_B200_UNSUPPORTED = 2,     /* `unsupported_lowering` (docs/core/backend-support.md:73-75) */
+    AFFON_B200_CUDA_ERROR = 3,      /* a CUDA runtime call failed */
+    AFFON_B200_TIMEOUT = 4,         /* a bounded wait gave up (tensor-parallel path) */
+    AFFON_B200_GUARD_MISMATCH = 5,  /* denseInputs guard (docs/core/optimization-and-profiling.md:143-151) */
+    AFFON_B200_POLICY_REJECTED = 6, /* numericalPolicy rejects the candidate's class (quantized-inference.md:175-177) */
+    AFFON_B200_INVALID_ARG = 7,     /* null pointer, unknown enum, bad context */
+    AFFON_B200_INVALID_DTYPE = 8    /* program.ts:487 dtype rule */
+} affon_b200_status;
+
+typedef enum affon_b200_dtype {
+    AFFON_B200_F32 = 0,
+    AFFON_B200_BF16 = 1,
+    AFFON_B200_U32 = 2
+} affon_b200_dtype;
+
+/* CompileOptions.numericalPolicy (docs/core/optimization-and-profiling.md:124-130). */
+typedef enum affon_b200_policy {
+    AFFON_B200_POLICY_BACKEND_EQUIVALENT = 0, /* default: accepts `reassociated` */
+    AFFON_B200_POLICY_EXACT_ONLY = 1,         /* rejects every quantized candidate */
+    AFFON_B200_POLICY_APPROXIMATE = 2         /* also accepts bf16-rounded weights */
+} affon_b200_policy;
+
+/* Numerical class of a physical implementation. */
+typedef enum affon_b200_numerics {
+    AFFON_B200_EXACT = 0,
+    AFFON_B200_REASSOCIATED = 1,
+    AFFON_B200_APPROXIMATE = 2
+} affon_b200_numerics;
+
+/* A logical rank-two view: shape, element strides and a byte offset from the
+ * base pointer (quantized-inference.md:51-52: "logical indices are mapped
+ * through their element strides and byte offsets"). */
+typedef struct affon_b200_view {
+    int64_t rows;
+    int64_t cols;
+    int64_t row_stride;  /* elements */
+    int64_t col_stride;  /* elements */
+    int64_t byte_offset; /* bytes from the base pointer */
+} affon_b200_view;
+
+/* One quantized_matmul node: y[M,N] = x[M,K] . decode(w)[N,K]^T with
+ * decode(w)[n,k] = s[n,k/g] * q[n,k] + b[n,k/g] (quantized-inference.md:59-61).
+ * x: [M,K] f32|bf16; w: [N,K*bits/32] u32; s, b: [N,K/g] f32|bf16 (same dtype);
+ * y: [M,N] f32 (the reference result dtype, program.ts:494) or bf16
+ * (an extension for decoder use; selecting it opts into bf16 rounding). */
+typedef struct affon_b200_qmm_desc {
+    uint32_t struct_size;     /* sizeof(affon_b200_qmm_desc) */
+    int32_t bits;             /* 2, 4 or 8 */
+    int64_t group_size;       /* positive */
+    int32_t x_dtype;          /* affon_b200_dtype */
+    int32_t param_dtype;      /* dtype of scales and biases */
+    int32_t y_dtype;          /* AFFON_B200_F32 (default) or AFFON_B200_BF16 */
+    int32_t numerical_policy; /* affon_b200_policy */
+    int32_t dense_inputs;     /* nonzero: every input must be dense with zero offset */
+    int32_t reserved;
+    affon_b200_view x, w, s, b, y;
+} affon_b200_qmm_desc;
+
+/* Result of physical selection (the compute core's `implementation_id`,
+ * docs/core/optimization-and-profiling.md:369-380). */
+typedef struct affon_b200_selection {
+    char implementation_id[64]; /* e.g. "cuda_quantized_matmul.sm100_qmv_b4_g64" */
+    int32_t implementation_version;
+    int32_t numerical_class;    /* affon_b200_numerics */
+    int32_t splits;             /* split-K factor the launch will use (1 = none) */
+    int32_t reserved;
+    char reason[256];
+} affon_b200_selection;
+
+typedef struct affon_b200_ctx affon_b200_ctx;
+
+/* Library / device identification. */
+int affon_b200_abi_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+const char *affon_b200_last_error(void);
+
+/* Context: one per (device, stream).  device_ordinal < 0 reads
+ * AFFON_CUDA_DEVICE (docs/runtime/configuration.md:19,99-104; default 0).
+ * cuda_stream is a cudaStream_t (NULL = legacy default stream).  The context
+ * owns a split-K workspace; calls on one context must not overlap on the GPU
+ * from different streams. */
+int affon_b200_ctx_create(int device_ordinal, void *cuda_stream, affon_b200_ctx **out);
+int affon_b200_ctx_destroy(affon_b200_ctx *ctx);
+int affon_b200_ctx_set_stream(affon_b200_ctx *ctx, void *cuda_stream);
+int affon_b200_ctx_device(const affon_b200_ctx *ctx);
+/* Grow the workspace to at least `bytes` (allocates; never called implicitly
+ * by a launch, so launches can be captured in CUDA graphs). */
+int affon_b200_ctx_reserve_workspace(affon_b200_ctx *ctx, size_t bytes);
+
+/* Validation alone (program.ts:481-495 plus the descriptor's own checks). */
+int affon_b200_validate(const affon_b200_qmm_desc *desc);
+
+/* Physical selection without launching.  Replaces the compute core's
+ * candidate discovery -> numerical-policy filter -> implementation choice
+ * for quantized_matmul (quantized-inference.md:132-140,175-181). */
+int affon_b200_select(const affon_b200_qmm_desc *desc, affon_b200_selection *out);
+
+/* Launch quantized_matmul on the context's stream.  All pointers are device
+ * pointers (base of each view).  y is untouched when the call fails before
+ * the launch.  Replaces the reference's `cuda_quantized_matmul` backend
+ * kernel (quantized-inference.md:177-181). */
+int affon_b200_qmm(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
+                   const void *s, const void *b, void *y);
+
+/* Same with the selection the launch used reported in `sel` (may be NULL). */
+int affon_b200_qmm_explain(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
+                           const void *s, const void *b, void *y, affon_b200_selection *sel);
+
+/* Host-buffer form: copies the four inputs host->device, launches, copies y
+ * device->host and synchronises the context stream.  Staging buffers are
+ * owned by the context and reused across calls.  This is the synchronous
+ * caller-owned-host-buffer contract of compute_core_cyna.zig:1000-1032. */
+int affon_b200_qmm_host(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
+                        const void *s, const void *b, void *y);
+
+/* The reference's C-ABI shape (compute_core_cyna.zig:29-45) on the GPU:
+ * dense f32 activations / parameters / output, host buffers, element counts,
+ * synchronous.  Status 0 ok, 1 invalid shape (output untouched), other =
+ * core failure.  Uses a per-thread default context on AFFON_CUDA_DEVICE. */
+int affon_b200_compute_core_run_quantized_matmul_f32(
+    const float *activation, size_t activation_count, const uint32_t *weights, size_t weight_count,
+    const float *scales, size_t scale_count, const float *biases, size_t bias_count, float *output,
+    size_t output_count, size_t rows, size_t depth, size_t columns, size_t bits, size_t group_size);
+
+/* Number of kernel launches this library issued in this process (all
+ * contexts); lets callers and benchmarks count native launches. */
+uint64_t affon_b200_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AFFON_B200_H */
