@@ -42,6 +42,7 @@ SIGNATURES = {
     "affon_b200_ctx_set_stream": ([c_vp, c_vp], c_i32),
     "affon_b200_ctx_device": ([c_vp], c_i32),
     "affon_b200_ctx_reserve_workspace": ([c_vp, c_sz], c_i32),
+    "affon_b200_ctx_synchronize": ([c_vp], c_i32),
     "affon_b200_validate": ([ctypes.POINTER(QmmDesc)], c_i32),
     "affon_b200_select": ([ctypes.POINTER(QmmDesc), ctypes.POINTER(Selection)], c_i32),
     "affon_b200_qmm": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),

@@ -174,20 +174,23 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
     const bool qmv_ok = afb::qmv_supported(probe, &why_qmv);
     const char *why_tc = "";
     const bool tc_ok = afb::qmm_tc_supported(a, &why_tc);
-    if (qmv_ok && a.M <= 16) {
+    afb::QmvPlan qplan{};
+    if (qmv_ok) qplan = afb::qmv_plan(probe, num_sms, workspace);
+    const bool qmv_plannable = qmv_ok && qplan.splits > 0;
+    if (qmv_ok && !qmv_plannable) why_qmv = "qmv: activation slice does not fit shared memory";
+    if (qmv_plannable && a.M <= 16) {
         c.impl = IMPL_QMV;
-        c.plan = afb::qmv_plan(a, num_sms, workspace);
+        c.plan = qplan;
         snprintf(reason, sizeof reason, "M=%lld <= 16: decode qmv, split-K %d, %d CTAs per split", (long long)a.M,
                  c.plan.splits, c.plan.grid_n);
     } else if (tc_ok && (d->numerical_policy == AFFON_B200_POLICY_APPROXIMATE || a.y_bf16)) {
         c.impl = IMPL_QMM_TC;
         snprintf(reason, sizeof reason, "M=%lld >= 64: tcgen05 qmm with bf16-rounded decoded weights", (long long)a.M);
-    } else if (qmv_ok && a.M <= 64) {
+    } else if (qmv_plannable && (a.M <= 64 || d->numerical_policy != AFFON_B200_POLICY_APPROXIMATE)) {
         c.impl = IMPL_QMV;
         c.passes = static_cast<int>((a.M + 15) / 16);
-        c.plan = afb::qmv_plan(probe, num_sms, workspace);
-        snprintf(reason, sizeof reason, "16 < M=%lld <= 64: %d qmv passes over 16-row slices", (long long)a.M,
-                 c.passes);
+        c.plan = qplan;
+        snprintf(reason, sizeof reason, "M=%lld > 16: %d qmv passes over 16-row slices", (long long)a.M, c.passes);
     } else {
         snprintf(reason, sizeof reason, "generic strided kernel (%s%s%s)", why_qmv, tc_ok ? "" : "; ",
                  tc_ok ? "" : why_tc);
@@ -221,7 +224,8 @@ int launch(affon_b200_ctx *ctx, const afb::QmmArgs &a, const Choice &c) {
             slice.M = (a.M - m0) < 16 ? (a.M - m0) : 16;
             slice.x.ptr = static_cast<const char *>(a.x.ptr) + m0 * a.x.row_stride * 2;
             slice.y = static_cast<char *>(a.y) + m0 * a.ldy * (a.y_bf16 ? 2 : 4);
-            afb::QmvPlan plan = c.passes == 1 ? c.plan : afb::qmv_plan(slice, ctx->num_sms, ctx->workspace_bytes);
+            afb::QmvPlan plan = slice.M == 16 || c.passes == 1 ? c.plan
+                                                                : afb::qmv_plan(slice, ctx->num_sms, ctx->workspace_bytes);
             if (afb::qmv_workspace_bytes(slice, plan) > ctx->workspace_bytes)
                 return fail(AFFON_B200_CUDA_ERROR, "qmv plan exceeds the context workspace");
             e = afb::launch_qmv(slice, plan, ctx->workspace, ctx->stream);
@@ -329,6 +333,23 @@ int affon_b200_ctx_reserve_workspace(affon_b200_ctx *ctx, size_t bytes) {
     if ((e = cudaMemset(ctx->workspace, 0, bytes)) != cudaSuccess) return cuda_fail(e, "workspace cudaMemset");
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "workspace init");
     ctx->workspace_bytes = bytes;
+    return AFFON_B200_OK;
+}
+
+int affon_b200_ctx_synchronize(affon_b200_ctx *ctx) {
+    t_error.clear();
+    if (!ctx) return fail(AFFON_B200_INVALID_ARG, "null context");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = ctx->stream ? cudaStreamSynchronize(ctx->stream) : cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+    unsigned status = 0;
+    if ((e = cudaMemcpy(&status, ctx->workspace, sizeof status, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "status read");
+    if (status != 0) {
+        const unsigned zero = 0;
+        cudaMemcpy(ctx->workspace, &zero, sizeof zero, cudaMemcpyHostToDevice);
+        return fail(AFFON_B200_TIMEOUT, "a kernel gave up a bounded wait (device status %u)", status);
+    }
     return AFFON_B200_OK;
 }
 

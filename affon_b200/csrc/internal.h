@@ -28,11 +28,18 @@ cudaError_t launch_qmm_generic(const QmmArgs &a, cudaStream_t stream);
 
 // Decode qmv for M <= 16, bits in {4, 8}, group 64, bf16 x/s/b, dense rows.
 struct QmvPlan {
-    int splits;            // split-K factor (>= 1)
-    int blocks_per_split;  // pipeline blocks (4 groups each) per split
-    int grid_n;            // CTAs along N per split
+    int splits;      // split-K factor (>= 1; 0 = not plannable)
+    int ks;          // K per split
+    int grid_n;      // persistent CTAs
     int smem_bytes;
 };
+
+// Context workspace layout: [0, 256) device status words (a bounded wait that
+// gives up writes there); [kCounterOffset, kPartialOffset) split-K arrival
+// counters, zero between launches; [kPartialOffset, ...) f32 partial sums.
+constexpr size_t kCounterOffset = 256;
+constexpr int64_t kMaxTiles = 262144;
+constexpr size_t kPartialOffset = kCounterOffset + size_t(kMaxTiles) * 4;
 bool qmv_supported(const QmmArgs &a, const char **why);
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes);
 size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p);

@@ -3,97 +3,70 @@
 // activations / scales / biases, f32 accumulation (the layout and formula of
 // docs/core/quantized-inference.md:45-67).
 //
-// Why tensor cores at M <= 16: at the HBM rate of a B200 (~6.5 TB/s) a 4-bit
-// weight stream delivers ~11.6e12 weights/s; decoding each weight to a float
-// and multiplying it on the CUDA cores costs ~3 lane-ops, which is as much as
-// the 148 SMs can issue.  So each warp decodes its packed words in registers
-// straight into the A fragments of m16n8k16 bf16 MMAs (no shared-memory round
-// trip for the weights), with the activations as the B operand.
+// Streaming: a persistent CTA per SM.  One producer warp moves the packed
+// weight matrix through a ring of shared-memory stages with 2D TMA loads
+// (128 rows x 128 bytes per stage, 128-byte swizzle, plus the matching
+// 128 x 8 boxes of bf16 scales and biases), so up to STAGES x 20 KB per SM
+// are in flight without costing registers.  Consumer warps read the packed
+// words from shared memory, decode them in registers and feed tensor cores.
+//
+// Why tensor cores at M <= 16: at ~6.5 TB/s a 4-bit weight stream delivers
+// ~11.6e12 weights/s; decoding each weight to a float and multiplying it on
+// the CUDA cores costs ~3 lane-ops, as much as the 148 SMs can issue.  The
+// decoded codes go straight from registers into the A fragments of
+// m16n8k16 bf16 MMAs (weights as the 16-row A operand, activations as B).
 //
 // Exact codes, per-group affine in f32: the MMA multiplies the *integer codes*
-// q (exact in bf16) by x, giving C_g = sum_{k in g} x*q in f32.  The affine
+// q (exact in bf16) by x, giving C_g = sum_{k in g} x*q in f32; the affine
 // decode is applied per group of 64 outside the tensor core:
 //     y += s[n,g] * C_g + b[n,g] * X_g,   X_g = sum_{k in g} x[k]   (f32)
 // which is sum_k x*(s*q+b) up to reassociation; weights are never rounded to
 // bf16 (quantized-inference.md:119-121).  Numerical class: reassociated.
 //
-// Work decomposition: 16-row N tiles (one m16 MMA tile), one warp per tile.
-// K is cut into `splits` ranges; a CTA stages its range of x in shared memory
-// once (permuted into MMA-fragment order for 4-bit) together with X_g, then
-// its 8 warps stream their tiles' packed weights with 8/16-byte read-only
-// loads, software-pipelined over 256-K blocks.  With splits > 1 each warp
-// writes an f32 partial; the warp that completes a tile last (per-tile
-// arrival counter) sums the partials in split order and stores y, so results
-// do not depend on scheduling, and it resets the counter for the next launch.
+// Work units are (128-row block, K split).  A CTA takes a contiguous range of
+// units (split-major), stages its split's slice of x (4-bit: each 8-element
+// word permuted to match the nibble pairs the decoder produces) and the group
+// sums X_g in shared memory, then streams its blocks.  With splits > 1 each
+// warp writes f32 partials; the warp completing a tile last (per-tile arrival
+// counter in the workspace) sums them in split order, stores y and resets the
+// counter, so results do not depend on scheduling.
 #include <algorithm>
+#include <cmath>
 
 #include "common.cuh"
 #include "internal.h"
+#include "sm100.cuh"
 
 namespace afb {
 namespace qmv {
 
-constexpr int WARPS = 8;
-constexpr int THREADS = WARPS * 32;
 constexpr int GROUP = 64;
-constexpr int BG = 4;             // groups per pipeline block
-constexpr int BK = BG * GROUP;    // K per pipeline block
-constexpr int XS_PAD = 8;         // bf16 elements of padding per staged x row
+constexpr int ROWS = 128;                        // rows per block = TMA box height
+constexpr int W_BYTES = ROWS * 128;              // packed bytes per stage
+constexpr int SB_BYTES = ROWS * 16;              // one 8-group box of scales (or biases)
+constexpr int STAGE_BYTES = W_BYTES + 2 * SB_BYTES;
+constexpr int XS_PAD = 8;
+constexpr int STAGES = 6;
 
 struct Params {
     const uint16_t *x;
     int64_t ldx;
-    const uint32_t *w;
-    int64_t ldw;
-    const uint16_t *s;
-    int64_t lds;
-    const uint16_t *b;
-    int64_t ldb;
     void *y;
     int64_t ldy;
     float *partial;
     unsigned *counters;
-    int M, N;
-    int splits;
-    int blocks_per_split;
-    int tiles;
+    unsigned *status;
+    int M, N, K;
+    int splits, ks, nblocks, units;
     int y_bf16;
 };
 
 template <int BITS>
-struct Blk;
-template <>
-struct Blk<4> {
-    uint2 w[2][BG];  // rows g and g+8: two words (16 codes) per group
-    uint2 s[2], b[2];
+struct Shape {
+    static constexpr int GPS = BITS == 4 ? 4 : 2;         // groups per stage (128 packed bytes per row)
+    static constexpr int KPS = GPS * GROUP;                // K per stage
+    static constexpr int WORDS_PER_STAGE = 32;             // u32 words per row per stage
 };
-template <>
-struct Blk<8> {
-    uint4 w[2][BG];  // rows g and g+8: four words (16 codes) per group
-    uint2 s[2], b[2];
-};
-
-template <int BITS>
-__device__ __forceinline__ void load_block(Blk<BITS> &B, const Params &p, int64_t row0, int64_t row1, int G0, int t) {
-    constexpr int WPG = 2 * BITS;  // u32 words per row per group of 64
-    constexpr int TW = WPG / 4;    // words per thread per row per group
-    const uint32_t *r0 = p.w + row0 * p.ldw + static_cast<int64_t>(G0) * WPG + t * TW;
-    const uint32_t *r1 = p.w + row1 * p.ldw + static_cast<int64_t>(G0) * WPG + t * TW;
-#pragma unroll
-    for (int gi = 0; gi < BG; ++gi) {
-        if constexpr (BITS == 4) {
-            B.w[0][gi] = ldg_stream_v2(r0 + gi * WPG);
-            B.w[1][gi] = ldg_stream_v2(r1 + gi * WPG);
-        } else {
-            B.w[0][gi] = ldg_stream_v4(r0 + gi * WPG);
-            B.w[1][gi] = ldg_stream_v4(r1 + gi * WPG);
-        }
-    }
-    B.s[0] = ldg_nc_v2(p.s + row0 * p.lds + G0);
-    B.s[1] = ldg_nc_v2(p.s + row1 * p.lds + G0);
-    B.b[0] = ldg_nc_v2(p.b + row0 * p.ldb + G0);
-    B.b[1] = ldg_nc_v2(p.b + row1 * p.ldb + G0);
-}
 
 // Codes p and p+4 of a 4-bit word as an exact bf16 pair (128+q, then -128).
 __device__ __forceinline__ uint32_t dec4(uint32_t w, int p) {
@@ -106,81 +79,6 @@ __device__ __forceinline__ uint32_t dec8(uint32_t w, int i) {
     return pack_bf16x2(f0, f1);
 }
 
-__device__ __forceinline__ float bf16_lane(uint2 v, int i) {
-    uint32_t word = (i < 2) ? v.x : v.y;
-    return __uint_as_float((i & 1) ? (word & 0xFFFF0000u) : (word << 16));
-}
-
-template <int BITS, int MT>
-__device__ __forceinline__ void compute_block(const Blk<BITS> &B, float (&acc)[MT][4], const char *xs, int xs_rs,
-                                              const float *xg, int Gl0, int g, int t, int M) {
-#pragma unroll
-    for (int gi = 0; gi < BG; ++gi) {
-        const int Gl = Gl0 + gi;
-        uint32_t xf[MT][8];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-            const int m = g + 8 * mt;
-            if (m < M) {
-                const char *src = xs + m * xs_rs + (Gl * GROUP + 16 * t) * 2;
-                uint4 v0 = *reinterpret_cast<const uint4 *>(src);
-                uint4 v1 = *reinterpret_cast<const uint4 *>(src + 16);
-                xf[mt][0] = v0.x; xf[mt][1] = v0.y; xf[mt][2] = v0.z; xf[mt][3] = v0.w;
-                xf[mt][4] = v1.x; xf[mt][5] = v1.y; xf[mt][6] = v1.z; xf[mt][7] = v1.w;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xf[mt][i] = 0u;
-            }
-        }
-        float c[MT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint32_t a[4];
-            uint32_t b0[MT], b1[MT];
-            if constexpr (BITS == 4) {
-                const uint32_t w0 = (j < 2) ? B.w[0][gi].x : B.w[0][gi].y;
-                const uint32_t w1 = (j < 2) ? B.w[1][gi].x : B.w[1][gi].y;
-                const int p0 = 2 * (j & 1);
-                a[0] = dec4(w0, p0);
-                a[1] = dec4(w1, p0);
-                a[2] = dec4(w0, p0 + 1);
-                a[3] = dec4(w1, p0 + 1);
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    b0[mt] = xf[mt][4 * (j >> 1) + p0];
-                    b1[mt] = xf[mt][4 * (j >> 1) + p0 + 1];
-                }
-            } else {
-                const uint32_t w0 = (j == 0) ? B.w[0][gi].x : (j == 1) ? B.w[0][gi].y : (j == 2) ? B.w[0][gi].z : B.w[0][gi].w;
-                const uint32_t w1 = (j == 0) ? B.w[1][gi].x : (j == 1) ? B.w[1][gi].y : (j == 2) ? B.w[1][gi].z : B.w[1][gi].w;
-                a[0] = dec8(w0, 0);
-                a[1] = dec8(w1, 0);
-                a[2] = dec8(w0, 2);
-                a[3] = dec8(w1, 2);
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    b0[mt] = xf[mt][2 * j];
-                    b1[mt] = xf[mt][2 * j + 1];
-                }
-            }
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) mma_bf16_16816(c[mt], a, b0[mt], b1[mt], c[mt]);
-        }
-        const float s0 = bf16_lane(B.s[0], gi), s1 = bf16_lane(B.s[1], gi);
-        const float q0 = bf16_lane(B.b[0], gi), q1 = bf16_lane(B.b[1], gi);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-            const float2 X = *reinterpret_cast<const float2 *>(xg + Gl * 16 + 2 * t + 8 * mt);
-            acc[mt][0] = fmaf(s0, c[mt][0], fmaf(q0, X.x, acc[mt][0]));
-            acc[mt][1] = fmaf(s0, c[mt][1], fmaf(q0, X.y, acc[mt][1]));
-            acc[mt][2] = fmaf(s1, c[mt][2], fmaf(q1, X.x, acc[mt][2]));
-            acc[mt][3] = fmaf(s1, c[mt][3], fmaf(q1, X.y, acc[mt][3]));
-        }
-    }
-}
-
 __device__ __forceinline__ void store_out(const Params &p, int m, int64_t n, float v) {
     if (p.y_bf16)
         static_cast<uint16_t *>(p.y)[m * p.ldy + n] = f32_to_bf16_bits(v);
@@ -189,9 +87,10 @@ __device__ __forceinline__ void store_out(const Params &p, int m, int64_t n, flo
 }
 
 template <int MT>
-__device__ __forceinline__ void tile_epilogue(const Params &p, float (&acc)[MT][4], int tile, int split, int g, int t,
-                                              int lane) {
+__device__ __forceinline__ void tile_epilogue(const Params &p, const float (&acc)[MT][4], int tile, int split, int g,
+                                              int t, int lane) {
     const int64_t n0 = static_cast<int64_t>(tile) * 16;
+    if (n0 >= p.N) return;
     if (p.splits == 1) {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
@@ -226,7 +125,8 @@ __device__ __forceinline__ void tile_epilogue(const Params &p, float (&acc)[MT][
             const int64_t n = n0 + g + 8 * (i >> 1);
             if (m < p.M && n < p.N) {
                 float sum = 0.0f;
-                for (int sp = 0; sp < p.splits; ++sp) sum += __ldcg(&p.partial[(static_cast<int64_t>(sp) * p.M + m) * p.N + n]);
+                for (int sp = 0; sp < p.splits; ++sp)
+                    sum += __ldcg(&p.partial[(static_cast<int64_t>(sp) * p.M + m) * p.N + n]);
                 store_out(p, m, n, sum);
             }
         }
@@ -234,28 +134,17 @@ __device__ __forceinline__ void tile_epilogue(const Params &p, float (&acc)[MT][
     if (lane == 0) atomicExch(&p.counters[tile], 0u);
 }
 
-template <int BITS, int MT, int STAGES>
-__global__ void __launch_bounds__(THREADS, 1) qmv_kernel(Params p) {
-    extern __shared__ __align__(16) char smem[];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int split = blockIdx.y;
-    const int nb = p.blocks_per_split;
-    const int Ks = nb * BK;
-    const int Gs = Ks / GROUP;
-    const int64_t k0 = static_cast<int64_t>(split) * Ks;
-    const int xs_rs = (Ks + XS_PAD) * 2;
-    char *xs = smem;
-    float *xg = reinterpret_cast<float *>(smem + static_cast<size_t>(p.M) * xs_rs);
-
-    // Stage x[:, k0:k0+Ks) (4-bit: each 8-element word permuted to
-    // [x0 x4 x1 x5 x2 x6 x3 x7] so that B fragments match the nibble pairs
-    // dec4 produces) and the per-group sums X_g.
-    for (int i = tid; i < Gs * 16; i += THREADS) xg[i] = 0.0f;
-    __syncthreads();
-    const int cpr = Ks / 8;  // 16-byte chunks per row
+// Stage x[:, k0:k0+ks) (and the group sums X_g) into shared memory; run by
+// the consumer warps only.
+template <int BITS>
+__device__ __forceinline__ void stage_x(const Params &p, char *xs, float *xg, int xs_rs, int64_t k0, int tid,
+                                        int nthreads) {
+    const int gs = p.ks / GROUP;
+    for (int i = tid; i < gs * 16; i += nthreads) xg[i] = 0.0f;
+    named_bar_sync(1, nthreads);
+    const int cpr = p.ks / 8;  // 16-byte chunks per row
     const int total = p.M * cpr;
-    for (int base = 0; base < total; base += THREADS) {
+    for (int base = 0; base < total; base += nthreads) {
         const int c = base + tid;
         const bool valid = c < total;
         const int m = valid ? c / cpr : 0, kc = valid ? c % cpr : 0;
@@ -280,82 +169,183 @@ __global__ void __launch_bounds__(THREADS, 1) qmv_kernel(Params p) {
             if ((kc & 7) == 0) xg[(kc >> 3) * 16 + m] = sum;
         }
     }
+    named_bar_sync(1, nthreads);
+}
+
+template <int BITS, int MT, int NT>
+__global__ void __launch_bounds__(32 * (8 / NT + 1), 1)
+    qmv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+               const __grid_constant__ CUtensorMap bmap, Params p) {
+    constexpr int CW = 8 / NT;  // consumer warps; each owns NT 16-row tiles of the 128-row block
+    constexpr int GPS = Shape<BITS>::GPS;
+    extern __shared__ char smem_raw[];
+    char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    char *ring = smem;
+    const int xs_rs = (p.ks + XS_PAD) * 2;
+    char *xs = ring + STAGES * STAGE_BYTES;
+    float *xg = reinterpret_cast<float *>(xs + p.M * xs_rs);
+    uint64_t *full = reinterpret_cast<uint64_t *>(xg + (p.ks / GROUP) * 16);
+    uint64_t *empty = full + STAGES;
+    volatile int *abort = reinterpret_cast<volatile int *>(empty + STAGES);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], CW);
+        }
+        *abort = 0;
+        fence_mbar_init();
+    }
     __syncthreads();
 
-    const int stride = gridDim.x * WARPS;
-    const int tile0 = blockIdx.x * WARPS + warp;
-    const int my_tiles = tile0 < p.tiles ? (p.tiles - 1 - tile0) / stride + 1 : 0;
-    const int total_steps = my_tiles * nb;
-    if (total_steps == 0) return;
+    const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.units / gridDim.x);
+    const int u_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.units / gridDim.x);
+    const int nst = p.ks / Shape<BITS>::KPS;  // stages per unit
 
-    const int gbase = split * nb * BG;  // first absolute group of this split
-    auto rows_of = [&](int step, int64_t &r0, int64_t &r1, int &blk, int &tile) {
-        const int ti = step / nb;
-        blk = step - ti * nb;
-        tile = tile0 + ti * stride;
-        const int64_t n0 = static_cast<int64_t>(tile) * 16;
-        r0 = min(n0 + g, static_cast<int64_t>(p.N - 1));
-        r1 = min(n0 + g + 8, static_cast<int64_t>(p.N - 1));
-    };
-
-    Blk<BITS> buf[STAGES];
-#pragma unroll
-    for (int st = 0; st < STAGES; ++st) {
-        if (st < total_steps) {
-            int64_t r0, r1;
-            int blk, tile;
-            rows_of(st, r0, r1, blk, tile);
-            load_block<BITS>(buf[st], p, r0, r1, gbase + blk * BG, t);
-        }
-    }
-    float acc[MT][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
-
-    for (int step = 0; step < total_steps; step += STAGES) {
-#pragma unroll
-        for (int st = 0; st < STAGES; ++st) {
-            const int s = step + st;
-            if (s < total_steps) {
-                int64_t r0, r1;
-                int blk, tile;
-                rows_of(s, r0, r1, blk, tile);
-                compute_block<BITS, MT>(buf[st], acc, xs, xs_rs, xg, blk * BG, g, t, p.M);
-                if (s + STAGES < total_steps) {
-                    int64_t q0, q1;
-                    int qb, qt;
-                    rows_of(s + STAGES, q0, q1, qb, qt);
-                    load_block<BITS>(buf[st], p, q0, q1, gbase + qb * BG, t);
-                }
-                if (blk == nb - 1) {
-                    tile_epilogue<MT>(p, acc, tile, split, g, t, lane);
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
+    if (warp == CW) {  // ------------------------------------------ producer
+        if (lane == 0) {
+            tma_prefetch_desc(&wmap);
+            tma_prefetch_desc(&smap);
+            tma_prefetch_desc(&bmap);
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int u = u_begin; u < u_end; ++u) {
+                const int split = u / p.nblocks, blk = u - split * p.nblocks;
+                const int64_t k0 = static_cast<int64_t>(split) * p.ks;
+                for (int j = 0; j < nst; ++j) {
+                    // On a timed-out wait (abort set) stop issuing loads; consumers drain.
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) return;
+                    char *dst = ring + stage * STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                    const int64_t kk = k0 + static_cast<int64_t>(j) * Shape<BITS>::KPS;
+                    tma_load_2d(dst, &wmap, &full[stage], static_cast<int>(kk * BITS / 32), blk * ROWS);
+                    const int g8 = static_cast<int>((kk / GROUP) & ~int64_t(7));
+                    tma_load_2d(dst + W_BYTES, &smap, &full[stage], g8, blk * ROWS);
+                    tma_load_2d(dst + W_BYTES + SB_BYTES, &bmap, &full[stage], g8, blk * ROWS);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
             }
         }
+        return;
     }
-}
 
-template <int BITS, int MT, int STAGES>
-cudaError_t launch_cfg(const Params &p, const QmvPlan &plan, cudaStream_t stream) {
-    auto kern = qmv_kernel<BITS, MT, STAGES>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
-    if (e != cudaSuccess) return e;
-    // Size the grid to the resident CTAs (registers and shared memory both
-    // limit it), so every split's CTAs run in one wave and warps loop over tiles.
-    int per_sm = 1, dev = 0, sms = 148;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, THREADS, plan.smem_bytes)) != cudaSuccess)
-        return e;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    const int64_t ctas_needed = (p.tiles + WARPS - 1) / WARPS;
-    const int64_t slots = static_cast<int64_t>(sms) * (per_sm > 0 ? per_sm : 1);
-    const int grid_n = static_cast<int>(std::max<int64_t>(1, std::min(ctas_needed, (slots + plan.splits - 1) / plan.splits)));
-    dim3 grid(grid_n, plan.splits);
-    kern<<<grid, THREADS, plan.smem_bytes, stream>>>(p);
-    count_launch();
-    return cudaGetLastError();
+    // ------------------------------------------------------------ consumers
+    const int g = lane >> 2, t = lane & 3;
+    int stage = 0;
+    uint32_t phase = 0;
+    int cur_split = -1;
+    for (int u = u_begin; u < u_end; ++u) {
+        const int split = u / p.nblocks, blk = u - split * p.nblocks;
+        if (split != cur_split) {
+            named_bar_sync(1, CW * 32);
+            stage_x<BITS>(p, xs, xg, xs_rs, static_cast<int64_t>(split) * p.ks, tid, CW * 32);
+            cur_split = split;
+        }
+        float acc[NT][MT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) acc[nt][mt][0] = acc[nt][mt][1] = acc[nt][mt][2] = acc[nt][mt][3] = 0.f;
+
+        for (int j = 0; j < nst; ++j) {
+            // A timed-out wait sets *abort; keep walking the loop (results are
+            // then garbage and the status word says TIMEOUT) so that every
+            // consumer reaches the same named barriers and no thread hangs.
+            mbar_wait(&full[stage], phase, abort, p.status);
+            const char *sw = ring + stage * STAGE_BYTES;
+            const char *ssb = sw + W_BYTES;
+            const char *bsb = ssb + SB_BYTES;
+#pragma unroll
+            for (int G = 0; G < GPS; ++G) {
+                const int Gl = j * GPS + G;           // group index within the split
+                const int go = Gl & 7;                // index within the 8-group scale box
+                uint32_t xf[MT][8];
+                float2 X[MT];
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    const int m = g + 8 * mt;
+                    if (m < p.M) {
+                        const char *src = xs + m * xs_rs + (Gl * GROUP + 16 * t) * 2;
+                        const uint4 v0 = *reinterpret_cast<const uint4 *>(src);
+                        const uint4 v1 = *reinterpret_cast<const uint4 *>(src + 16);
+                        xf[mt][0] = v0.x; xf[mt][1] = v0.y; xf[mt][2] = v0.z; xf[mt][3] = v0.w;
+                        xf[mt][4] = v1.x; xf[mt][5] = v1.y; xf[mt][6] = v1.z; xf[mt][7] = v1.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) xf[mt][i] = 0u;
+                    }
+                    X[mt] = *reinterpret_cast<const float2 *>(xg + Gl * 16 + 2 * t + 8 * mt);
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int r0 = (warp * NT + nt) * 16 + g;  // block row of this thread (and r0 + 8)
+                    uint32_t w0[4], w1[4];
+                    if constexpr (BITS == 4) {
+                        const int off = (((2 * G + (t >> 1)) ^ g) << 4) + (t & 1) * 8;
+                        const uint2 a = *reinterpret_cast<const uint2 *>(sw + r0 * 128 + off);
+                        const uint2 b = *reinterpret_cast<const uint2 *>(sw + (r0 + 8) * 128 + off);
+                        w0[0] = a.x; w0[1] = a.y; w1[0] = b.x; w1[1] = b.y;
+                    } else {
+                        const int off = ((4 * G + t) ^ g) << 4;
+                        const uint4 a = *reinterpret_cast<const uint4 *>(sw + r0 * 128 + off);
+                        const uint4 b = *reinterpret_cast<const uint4 *>(sw + (r0 + 8) * 128 + off);
+                        w0[0] = a.x; w0[1] = a.y; w0[2] = a.z; w0[3] = a.w;
+                        w1[0] = b.x; w1[1] = b.y; w1[2] = b.z; w1[3] = b.w;
+                    }
+                    const float s0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ssb + r0 * 16 + go * 2));
+                    const float s1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ssb + (r0 + 8) * 16 + go * 2));
+                    const float q0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(bsb + r0 * 16 + go * 2));
+                    const float q1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(bsb + (r0 + 8) * 16 + go * 2));
+                    float c[MT][4];
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        uint32_t a[4], b0[MT], b1[MT];
+                        if constexpr (BITS == 4) {
+                            const int p0 = 2 * (s & 1);
+                            const uint32_t u0 = w0[s >> 1], u1 = w1[s >> 1];
+                            a[0] = dec4(u0, p0);
+                            a[1] = dec4(u1, p0);
+                            a[2] = dec4(u0, p0 + 1);
+                            a[3] = dec4(u1, p0 + 1);
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt) {
+                                b0[mt] = xf[mt][4 * (s >> 1) + p0];
+                                b1[mt] = xf[mt][4 * (s >> 1) + p0 + 1];
+                            }
+                        } else {
+                            a[0] = dec8(w0[s], 0);
+                            a[1] = dec8(w1[s], 0);
+                            a[2] = dec8(w0[s], 2);
+                            a[3] = dec8(w1[s], 2);
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt) {
+                                b0[mt] = xf[mt][2 * s];
+                                b1[mt] = xf[mt][2 * s + 1];
+                            }
+                        }
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) mma_bf16_16816(c[mt], a, b0[mt], b1[mt], c[mt]);
+                    }
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        acc[nt][mt][0] = fmaf(s0, c[mt][0], fmaf(q0, X[mt].x, acc[nt][mt][0]));
+                        acc[nt][mt][1] = fmaf(s0, c[mt][1], fmaf(q0, X[mt].y, acc[nt][mt][1]));
+                        acc[nt][mt][2] = fmaf(s1, c[mt][2], fmaf(q1, X[mt].x, acc[nt][mt][2]));
+                        acc[nt][mt][3] = fmaf(s1, c[mt][3], fmaf(q1, X[mt].y, acc[nt][mt][3]));
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            tile_epilogue<MT>(p, acc[nt], blk * (ROWS / 16) + warp * NT + nt, split, g, t, lane);
+    }
 }
 
 }  // namespace qmv
@@ -366,89 +356,101 @@ bool qmv_supported(const QmmArgs &a, const char **why) {
     if (a.group != 64) return no("qmv: group_size must be 64");
     if (!a.x_bf16 || !a.p_bf16) return no("qmv: activations and parameters must be bf16");
     if (a.M > 16) return no("qmv: M > 16");
-    if (a.K % qmv::BK) return no("qmv: K must be a multiple of 256");
+    if (a.K % 512) return no("qmv: K must be a multiple of 512");
     if (a.x.col_stride != 1 || a.w.col_stride != 1 || a.s.col_stride != 1 || a.b.col_stride != 1)
         return no("qmv: inputs need unit column stride");
     auto al = [](const void *p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
     if (!al(a.x.ptr, 16) || a.x.row_stride % 8) return no("qmv: x rows must be 16-byte aligned");
-    const int wal = a.bits == 8 ? 16 : 8;
-    if (!al(a.w.ptr, wal) || (a.w.row_stride * 4) % wal) return no("qmv: packed rows misaligned");
-    if (!al(a.s.ptr, 8) || !al(a.b.ptr, 8) || a.s.row_stride % 4 || a.b.row_stride % 4)
-        return no("qmv: parameter rows must be 8-byte aligned");
-    if (a.N >= (int64_t(1) << 31) / 16 || a.K >= (int64_t(1) << 30)) return no("qmv: size beyond 32-bit tile indexing");
+    if (!al(a.w.ptr, 16) || (a.w.row_stride * 4) % 16) return no("qmv: packed rows must be 16-byte aligned");
+    if (!al(a.s.ptr, 16) || !al(a.b.ptr, 16) || (a.s.row_stride * 2) % 16 || (a.b.row_stride * 2) % 16)
+        return no("qmv: parameter rows must be 16-byte aligned");
+    if ((a.N + 15) / 16 > kMaxTiles) return no("qmv: N beyond the arrival-counter region");
+    if (a.N >= (int64_t(1) << 31) || a.K >= (int64_t(1) << 30)) return no("qmv: size beyond 32-bit indexing");
     return true;
 }
 
-static int qmv_smem(const QmmArgs &a, int splits) {
-    const int64_t Ks = a.K / splits;
-    return static_cast<int>(a.M * (Ks + qmv::XS_PAD) * 2 + (Ks / qmv::GROUP) * 16 * 4);
+static int qmv_smem(const QmmArgs &a, int ks) {
+    return 1024 + qmv::STAGES * qmv::STAGE_BYTES + static_cast<int>(a.M) * (ks + qmv::XS_PAD) * 2 + (ks / 64) * 16 * 4 +
+           2 * qmv::STAGES * 8 + 16;
 }
 
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
-    const int nblk = static_cast<int>(a.K / qmv::BK);
-    const int64_t tiles = (a.N + 15) / 16;
-    const int smem_cap = 100 * 1024;
-    const int64_t target = static_cast<int64_t>(num_sms) * 12;  // warps wanted in flight
+    const int nk = static_cast<int>(a.K / 512);
+    const int64_t nblocks = (a.N + qmv::ROWS - 1) / qmv::ROWS;
+    const int smem_cap = 227 * 1024;
     auto ws_ok = [&](int s) {
-        return s == 1 || static_cast<size_t>(s) * a.M * a.N * 4 + tiles * 4 + 256 <= workspace_bytes;
+        return s == 1 || kPartialOffset + static_cast<size_t>(s) * a.M * a.N * 4 <= workspace_bytes;
     };
-    int chosen = 0;
-    for (int s = 1; s <= nblk; ++s) {
-        if (nblk % s || qmv_smem(a, s) > smem_cap || !ws_ok(s)) continue;
-        chosen = s;
-        if (tiles * s >= target && nblk / s >= 2) break;
-        if (tiles * s >= target) break;
-    }
-    if (chosen == 0) {  // smallest split that fits shared memory, ignoring parallelism
-        for (int s = 1; s <= nblk; ++s)
-            if (nblk % s == 0 && qmv_smem(a, s) <= 220 * 1024 && ws_ok(s)) { chosen = s; break; }
-    }
+    int smin = 0;
+    for (int s = 1; s <= nk; ++s)
+        if (nk % s == 0 && qmv_smem(a, static_cast<int>(a.K / s)) <= smem_cap) { smin = s; break; }
     QmvPlan p{};
-    p.splits = chosen > 0 ? chosen : 1;
-    p.blocks_per_split = nblk / p.splits;
-    p.smem_bytes = qmv_smem(a, p.splits);
-    const int per_sm = std::max(1, std::min(2, (220 * 1024) / std::max(1, p.smem_bytes)));
-    const int64_t ctas_needed = (tiles + qmv::WARPS - 1) / qmv::WARPS;
-    const int64_t slots = static_cast<int64_t>(num_sms) * per_sm;
-    p.grid_n = static_cast<int>(std::max<int64_t>(1, std::min(ctas_needed, (slots + p.splits - 1) / p.splits)));
+    if (smin == 0) return p;  // splits == 0: not plannable
+    double best = -1.0;
+    int best_s = smin;
+    for (int s = smin; s <= nk; ++s) {
+        if (nk % s || !ws_ok(s)) continue;
+        const int64_t units = nblocks * s;
+        const int64_t waves = (units + num_sms - 1) / num_sms;
+        const double eff = static_cast<double>(units) / static_cast<double>(waves * num_sms);
+        const double score = eff * (1.0 - 0.03 * std::log2(static_cast<double>(s) / smin));
+        if (score > best + 1e-9) { best = score; best_s = s; }
+    }
+    p.splits = best_s;
+    p.ks = static_cast<int>(a.K / best_s);
+    p.smem_bytes = qmv_smem(a, p.ks);
+    p.grid_n = static_cast<int>(std::min<int64_t>(num_sms, nblocks * best_s));
     return p;
 }
 
 size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p) {
     if (p.splits <= 1) return 0;
-    const int64_t tiles = (a.N + 15) / 16;
-    return static_cast<size_t>(p.splits) * a.M * a.N * 4 + static_cast<size_t>(tiles) * 4 + 256;
+    return kPartialOffset + static_cast<size_t>(p.splits) * a.M * a.N * 4;
+}
+
+template <int BITS, int MT, int NT>
+static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, const CUtensorMap &bm,
+                              const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream) {
+    auto kern = qmv::qmv_kernel<BITS, MT, NT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
+    if (e != cudaSuccess) return e;
+    kern<<<plan.grid_n, 32 * (8 / NT + 1), plan.smem_bytes, stream>>>(wm, sm, bm, p);
+    count_launch();
+    return cudaGetLastError();
 }
 
 cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, cudaStream_t stream) {
+    if (plan.splits < 1) return cudaErrorInvalidValue;
     qmv::Params p{};
     p.x = static_cast<const uint16_t *>(a.x.ptr);
     p.ldx = a.x.row_stride;
-    p.w = static_cast<const uint32_t *>(a.w.ptr);
-    p.ldw = a.w.row_stride;
-    p.s = static_cast<const uint16_t *>(a.s.ptr);
-    p.lds = a.s.row_stride;
-    p.b = static_cast<const uint16_t *>(a.b.ptr);
-    p.ldb = a.b.row_stride;
     p.y = a.y;
     p.ldy = a.ldy;
     p.M = static_cast<int>(a.M);
     p.N = static_cast<int>(a.N);
+    p.K = static_cast<int>(a.K);
     p.splits = plan.splits;
-    p.blocks_per_split = plan.blocks_per_split;
-    p.tiles = static_cast<int>((a.N + 15) / 16);
+    p.ks = plan.ks;
+    p.nblocks = static_cast<int>((a.N + qmv::ROWS - 1) / qmv::ROWS);
+    p.units = p.nblocks * p.splits;
     p.y_bf16 = a.y_bf16;
-    if (plan.splits > 1) {
-        // Workspace layout: [tiles] arrival counters (kept at zero between
-        // launches), then [splits][M][N] f32 partials at a 256-byte boundary.
-        p.counters = static_cast<unsigned *>(workspace);
-        size_t off = ((static_cast<size_t>(p.tiles) * 4 + 255) / 256) * 256;
-        p.partial = reinterpret_cast<float *>(static_cast<char *>(workspace) + off);
-    }
+    char *ws = static_cast<char *>(workspace);
+    p.status = reinterpret_cast<unsigned *>(ws);
+    p.counters = reinterpret_cast<unsigned *>(ws + kCounterOffset);
+    p.partial = reinterpret_cast<float *>(ws + kPartialOffset);
+    CUtensorMap wm, sm, bm;
+    const uint64_t words = static_cast<uint64_t>(a.K) * a.bits / 32;
+    if (!encode_tensor_map_2d(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32,
+                              qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tensor_map_2d(&sm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2, 8,
+                              qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_tensor_map_2d(&bm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2, 8,
+                              qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
     const bool mt2 = a.M > 8;
     if (a.bits == 4)
-        return mt2 ? qmv::launch_cfg<4, 2, 3>(p, plan, stream) : qmv::launch_cfg<4, 1, 3>(p, plan, stream);
-    return mt2 ? qmv::launch_cfg<8, 2, 2>(p, plan, stream) : qmv::launch_cfg<8, 1, 2>(p, plan, stream);
+        return mt2 ? launch_cfg<4, 2, 2>(wm, sm, bm, p, plan, stream) : launch_cfg<4, 1, 1>(wm, sm, bm, p, plan, stream);
+    return mt2 ? launch_cfg<8, 2, 2>(wm, sm, bm, p, plan, stream) : launch_cfg<8, 1, 1>(wm, sm, bm, p, plan, stream);
 }
 
 }  // namespace afb

@@ -124,6 +124,11 @@ int affon_b200_ctx_device(const affon_b200_ctx *ctx);
  * by a launch, so launches can be captured in CUDA graphs). */
 int affon_b200_ctx_reserve_workspace(affon_b200_ctx *ctx, size_t bytes);
 
+/* Wait for the context's stream and report device-side failures: returns
+ * AFFON_B200_TIMEOUT (and clears the flag) when a kernel's bounded wait gave
+ * up since the last check. */
+int affon_b200_ctx_synchronize(affon_b200_ctx *ctx);
+
 /* Validation alone (program.ts:481-495 plus the descriptor's own checks). */
 int affon_b200_validate(const affon_b200_qmm_desc *desc);
 
