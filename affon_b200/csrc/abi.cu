@@ -233,7 +233,7 @@ int launch(affon_b200_ctx *ctx, const afb::QmmArgs &a, const Choice &c) {
         break;
     }
     case IMPL_QMM_TC:
-        e = afb::launch_qmm_tc(a, ctx->stream);
+        e = afb::launch_qmm_tc(a, ctx->workspace, ctx->stream);
         break;
     default:
         e = afb::launch_qmm_generic(a, ctx->stream);

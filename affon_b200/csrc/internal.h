@@ -47,7 +47,7 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &p, void *workspace, cuda
 
 // Prefill qmm on tcgen05 tensor cores (M >= 64), bf16 x/s/b, 4/8-bit, group 64.
 bool qmm_tc_supported(const QmmArgs &a, const char **why);
-cudaError_t launch_qmm_tc(const QmmArgs &a, cudaStream_t stream);
+cudaError_t launch_qmm_tc(const QmmArgs &a, void *workspace, cudaStream_t stream);
 
 void count_launch(uint64_t n = 1);
 

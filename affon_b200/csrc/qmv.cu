@@ -6,8 +6,8 @@
 // Streaming: a persistent CTA per SM.  One producer warp moves the packed
 // weight matrix through a ring of shared-memory stages with 2D TMA loads
 // (128 rows x 128 bytes per stage, 128-byte swizzle, plus the matching
-// 128 x 8 boxes of bf16 scales and biases), so up to STAGES x 20 KB per SM
-// are in flight without costing registers.  Consumer warps read the packed
+// 128 x 8 boxes of bf16 scales and biases; 256-row stages when M > 8), so
+// 120-160 KB per SM are in flight without costing registers.  Consumer warps read the packed
 // words from shared memory, decode them in registers and feed tensor cores.
 //
 // Why tensor cores at M <= 16: at ~6.5 TB/s a 4-bit weight stream delivers
@@ -41,12 +41,19 @@ namespace afb {
 namespace qmv {
 
 constexpr int GROUP = 64;
-constexpr int ROWS = 128;                        // rows per block = TMA box height
-constexpr int W_BYTES = ROWS * 128;              // packed bytes per stage
-constexpr int SB_BYTES = ROWS * 16;              // one 8-group box of scales (or biases)
-constexpr int STAGE_BYTES = W_BYTES + 2 * SB_BYTES;
+constexpr int CW = 8;                            // consumer warps per CTA
 constexpr int XS_PAD = 8;
-constexpr int STAGES = 6;
+
+// Rows per block (= TMA box height) and ring geometry for NT 16-row tiles per
+// consumer warp.
+template <int NT>
+struct Ring {
+    static constexpr int ROWS = 128 * NT;
+    static constexpr int W_BYTES = ROWS * 128;   // packed bytes per stage
+    static constexpr int SB_BYTES = ROWS * 16;   // one 8-group box of scales (or biases)
+    static constexpr int STAGE_BYTES = W_BYTES + 2 * SB_BYTES;
+    static constexpr int STAGES = NT == 1 ? 6 : 4;
+};
 
 struct Params {
     const uint16_t *x;
@@ -68,9 +75,12 @@ struct Shape {
     static constexpr int WORDS_PER_STAGE = 32;             // u32 words per row per stage
 };
 
-// Codes p and p+4 of a 4-bit word as an exact bf16 pair (128+q, then -128).
+// Codes p and p+4 of a 4-bit word as the exact bf16 pair (128+q_p, 128+q_{p+4}).
+// The +128 offset is removed per group in f32: s*(C' - 128*X_g) + b*X_g =
+// s*C' + (b - 128*s)*X_g, evaluated inside one fma so the large terms cancel
+// exactly and only C' (the tensor-core sum) carries rounding.
 __device__ __forceinline__ uint32_t dec4(uint32_t w, int p) {
-    return bf16x2_sub(lop3_and_or(w >> (4 * p), 0x000F000Fu, 0x43004300u), 0x43004300u);
+    return lop3_and_or(p ? (w >> (4 * p)) : w, 0x000F000Fu, 0x43004300u);
 }
 // Bytes i and i+1 of an 8-bit word as an exact bf16 pair (via 2^23 + q in f32).
 __device__ __forceinline__ uint32_t dec8(uint32_t w, int i) {
@@ -173,10 +183,12 @@ __device__ __forceinline__ void stage_x(const Params &p, char *xs, float *xg, in
 }
 
 template <int BITS, int MT, int NT>
-__global__ void __launch_bounds__(32 * (8 / NT + 1), 1)
+__global__ void __launch_bounds__(32 * (CW + 1), 1)
     qmv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const __grid_constant__ CUtensorMap bmap, Params p) {
-    constexpr int CW = 8 / NT;  // consumer warps; each owns NT 16-row tiles of the 128-row block
+    using R = Ring<NT>;
+    constexpr int STAGES = R::STAGES, STAGE_BYTES = R::STAGE_BYTES, W_BYTES = R::W_BYTES, SB_BYTES = R::SB_BYTES;
+    constexpr int ROWS = R::ROWS;
     constexpr int GPS = Shape<BITS>::GPS;
     extern __shared__ char smem_raw[];
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -256,10 +268,27 @@ __global__ void __launch_bounds__(32 * (8 / NT + 1), 1)
             const char *sw = ring + stage * STAGE_BYTES;
             const char *ssb = sw + W_BYTES;
             const char *bsb = ssb + SB_BYTES;
+            const int go0 = (j * GPS) & 7;  // first group of this stage within the 8-group scale box
+            // Scales and biases of this stage for rows r0 and r0+8 of each tile:
+            // GPS bf16 per row (8 bytes for 4-bit, 4 bytes for 8-bit).
+            uint32_t sv[NT][2][GPS / 2], bv[NT][2][GPS / 2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int r = (warp * NT + nt) * 16 + g + 8 * h;
+                    if constexpr (GPS == 4) {
+                        const uint2 a = *reinterpret_cast<const uint2 *>(ssb + r * 16 + go0 * 2);
+                        const uint2 b = *reinterpret_cast<const uint2 *>(bsb + r * 16 + go0 * 2);
+                        sv[nt][h][0] = a.x; sv[nt][h][1] = a.y; bv[nt][h][0] = b.x; bv[nt][h][1] = b.y;
+                    } else {
+                        sv[nt][h][0] = *reinterpret_cast<const uint32_t *>(ssb + r * 16 + go0 * 2);
+                        bv[nt][h][0] = *reinterpret_cast<const uint32_t *>(bsb + r * 16 + go0 * 2);
+                    }
+                }
 #pragma unroll
             for (int G = 0; G < GPS; ++G) {
                 const int Gl = j * GPS + G;           // group index within the split
-                const int go = Gl & 7;                // index within the 8-group scale box
                 uint32_t xf[MT][8];
                 float2 X[MT];
 #pragma unroll
@@ -293,10 +322,16 @@ __global__ void __launch_bounds__(32 * (8 / NT + 1), 1)
                         w0[0] = a.x; w0[1] = a.y; w0[2] = a.z; w0[3] = a.w;
                         w1[0] = b.x; w1[1] = b.y; w1[2] = b.z; w1[3] = b.w;
                     }
-                    const float s0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ssb + r0 * 16 + go * 2));
-                    const float s1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(ssb + (r0 + 8) * 16 + go * 2));
-                    const float q0 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(bsb + r0 * 16 + go * 2));
-                    const float q1 = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(bsb + (r0 + 8) * 16 + go * 2));
+                    const uint32_t s_w0 = sv[nt][0][G >> 1], s_w1 = sv[nt][1][G >> 1];
+                    const uint32_t b_w0 = bv[nt][0][G >> 1], b_w1 = bv[nt][1][G >> 1];
+                    const float s0 = __uint_as_float((G & 1) ? (s_w0 & 0xFFFF0000u) : (s_w0 << 16));
+                    const float s1 = __uint_as_float((G & 1) ? (s_w1 & 0xFFFF0000u) : (s_w1 << 16));
+                    float q0 = __uint_as_float((G & 1) ? (b_w0 & 0xFFFF0000u) : (b_w0 << 16));
+                    float q1 = __uint_as_float((G & 1) ? (b_w1 & 0xFFFF0000u) : (b_w1 << 16));
+                    if constexpr (BITS == 4) {  // codes entered the MMA as 128+q
+                        q0 = fmaf(-128.0f, s0, q0);
+                        q1 = fmaf(-128.0f, s1, q1);
+                    }
                     float c[MT][4];
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
@@ -369,14 +404,23 @@ bool qmv_supported(const QmmArgs &a, const char **why) {
     return true;
 }
 
+struct RingGeom {
+    int rows, stages, stage_bytes;
+};
+static RingGeom ring_geom(const QmmArgs &a) {
+    if (a.M > 8) return {qmv::Ring<2>::ROWS, qmv::Ring<2>::STAGES, qmv::Ring<2>::STAGE_BYTES};
+    return {qmv::Ring<1>::ROWS, qmv::Ring<1>::STAGES, qmv::Ring<1>::STAGE_BYTES};
+}
+
 static int qmv_smem(const QmmArgs &a, int ks) {
-    return 1024 + qmv::STAGES * qmv::STAGE_BYTES + static_cast<int>(a.M) * (ks + qmv::XS_PAD) * 2 + (ks / 64) * 16 * 4 +
-           2 * qmv::STAGES * 8 + 16;
+    const RingGeom r = ring_geom(a);
+    return 1024 + r.stages * r.stage_bytes + static_cast<int>(a.M) * (ks + qmv::XS_PAD) * 2 + (ks / 64) * 16 * 4 +
+           2 * r.stages * 8 + 16;
 }
 
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     const int nk = static_cast<int>(a.K / 512);
-    const int64_t nblocks = (a.N + qmv::ROWS - 1) / qmv::ROWS;
+    const int64_t nblocks = (a.N + ring_geom(a).rows - 1) / ring_geom(a).rows;
     const int smem_cap = 227 * 1024;
     auto ws_ok = [&](int s) {
         return s == 1 || kPartialOffset + static_cast<size_t>(s) * a.M * a.N * 4 <= workspace_bytes;
@@ -412,15 +456,16 @@ template <int BITS, int MT, int NT>
 static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, const CUtensorMap &bm,
                               const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream) {
     auto kern = qmv::qmv_kernel<BITS, MT, NT>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(kern), plan.smem_bytes);
     if (e != cudaSuccess) return e;
-    kern<<<plan.grid_n, 32 * (8 / NT + 1), plan.smem_bytes, stream>>>(wm, sm, bm, p);
+    kern<<<plan.grid_n, 32 * (qmv::CW + 1), plan.smem_bytes, stream>>>(wm, sm, bm, p);
     count_launch();
     return cudaGetLastError();
 }
 
 cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, cudaStream_t stream) {
     if (plan.splits < 1) return cudaErrorInvalidValue;
+    const int rows = ring_geom(a).rows;
     qmv::Params p{};
     p.x = static_cast<const uint16_t *>(a.x.ptr);
     p.ldx = a.x.row_stride;
@@ -431,26 +476,26 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     p.K = static_cast<int>(a.K);
     p.splits = plan.splits;
     p.ks = plan.ks;
-    p.nblocks = static_cast<int>((a.N + qmv::ROWS - 1) / qmv::ROWS);
+    p.nblocks = static_cast<int>((a.N + rows - 1) / rows);
     p.units = p.nblocks * p.splits;
     p.y_bf16 = a.y_bf16;
     char *ws = static_cast<char *>(workspace);
     p.status = reinterpret_cast<unsigned *>(ws);
     p.counters = reinterpret_cast<unsigned *>(ws + kCounterOffset);
     p.partial = reinterpret_cast<float *>(ws + kPartialOffset);
-    CUtensorMap wm, sm, bm;
+    const CUtensorMap *wm, *sm, *bm;
     const uint64_t words = static_cast<uint64_t>(a.K) * a.bits / 32;
-    if (!encode_tensor_map_2d(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32,
-                              qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tensor_map_2d(&sm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2, 8,
-                              qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_tensor_map_2d(&bm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2, 8,
-                              qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32, rows,
+                                    CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        !(sm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2, 8,
+                                    rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+        !(bm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2, 8,
+                                    rows, CU_TENSOR_MAP_SWIZZLE_NONE)))
         return cudaErrorInvalidValue;
     const bool mt2 = a.M > 8;
     if (a.bits == 4)
-        return mt2 ? launch_cfg<4, 2, 2>(wm, sm, bm, p, plan, stream) : launch_cfg<4, 1, 1>(wm, sm, bm, p, plan, stream);
-    return mt2 ? launch_cfg<8, 2, 2>(wm, sm, bm, p, plan, stream) : launch_cfg<8, 1, 1>(wm, sm, bm, p, plan, stream);
+        return mt2 ? launch_cfg<4, 2, 2>(*wm, *sm, *bm, p, plan, stream) : launch_cfg<4, 1, 1>(*wm, *sm, *bm, p, plan, stream);
+    return mt2 ? launch_cfg<8, 2, 2>(*wm, *sm, *bm, p, plan, stream) : launch_cfg<8, 1, 1>(*wm, *sm, *bm, p, plan, stream);
 }
 
 }  // namespace afb

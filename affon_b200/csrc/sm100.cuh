@@ -12,7 +12,7 @@
 namespace afb {
 
 // Error word written by device code when a bounded wait gives up; the host
-// reads it through affon_b200_ctx_check().
+// reads it through affon_b200_ctx_synchronize().
 enum DeviceStatus : unsigned { DEV_OK = 0, DEV_TIMEOUT = 4 };
 
 AFB_DEVICE uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -153,4 +153,12 @@ namespace afb {
 bool encode_tensor_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner,
                           uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                           CUtensorMapSwizzle swizzle);
+// Same, memoised per argument tuple (a bounded process-wide cache), so
+// repeated launches on the same buffers skip the driver call.  The returned
+// map stays valid until the process exits.
+const CUtensorMap *cached_tensor_map_2d(CUtensorMapDataType dtype, const void *base, uint64_t inner, uint64_t outer,
+                                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                                        CUtensorMapSwizzle swizzle);
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device, size).
+cudaError_t ensure_smem_attr(const void *kernel, int bytes);
 }  // namespace afb
