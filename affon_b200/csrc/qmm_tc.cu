@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
         }
+        __syncwarp();  // reconverge before the CTA-wide barrier at the end
     } else if (warp == 2) {  // ------------------------------------ packed TMA
         if (lane == 0) {
             tma_prefetch_desc(&wmap);
@@ -164,6 +165,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
         }
+        __syncwarp();
     } else if (warp == 1) {  // ------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_bf16(BW, BX);
@@ -192,6 +194,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 umma_commit(&accfull[buf]);
             }
         }
+        __syncwarp();
     } else if (warp < 7) {  // ------------------------------------- dequantisers
         const int i = tid - 96;  // weight row within the tile
         int s = 0, ps_i = 0;
