@@ -47,7 +47,7 @@ int cuda_fail(cudaError_t e, const char *what) {
     return fail(AFFON_B200_CUDA_ERROR, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
-constexpr size_t kDefaultWorkspace = size_t(32) << 20;
+constexpr size_t kDefaultWorkspace = size_t(64) << 20;
 
 // Makes ctx->device current for the scope of one call.
 struct DeviceGuard {
@@ -177,7 +177,7 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
     afb::QmvPlan qplan{};
     if (qmv_ok) qplan = afb::qmv_plan(probe, num_sms, workspace);
     const bool qmv_plannable = qmv_ok && qplan.splits > 0;
-    if (qmv_ok && !qmv_plannable) why_qmv = "qmv: activation slice does not fit shared memory";
+    if (qmv_ok && !qmv_plannable) why_qmv = "qmv: no split fits shared memory and the context workspace";
     if (qmv_plannable && a.M <= 16) {
         c.impl = IMPL_QMV;
         c.plan = qplan;

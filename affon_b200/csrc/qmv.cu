@@ -52,7 +52,7 @@ struct Ring {
     static constexpr int W_BYTES = ROWS * 128;   // packed bytes per stage
     static constexpr int SB_BYTES = ROWS * 16;   // one 8-group box of scales (or biases)
     static constexpr int STAGE_BYTES = W_BYTES + 2 * SB_BYTES;
-    static constexpr int STAGES = NT == 1 ? 6 : 4;
+    static constexpr int STAGES = NT == 1 ? 6 : 3;
 };
 
 struct Params {
@@ -431,7 +431,7 @@ QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     QmvPlan p{};
     if (smin == 0) return p;  // splits == 0: not plannable
     double best = -1.0;
-    int best_s = smin;
+    int best_s = 0;
     for (int s = smin; s <= nk; ++s) {
         if (nk % s || !ws_ok(s)) continue;
         const int64_t units = nblocks * s;
@@ -440,6 +440,7 @@ QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
         const double score = eff * (1.0 - 0.03 * std::log2(static_cast<double>(s) / smin));
         if (score > best + 1e-9) { best = score; best_s = s; }
     }
+    if (best_s == 0) return p;  // no split fits the workspace: not plannable
     p.splits = best_s;
     p.ks = static_cast<int>(a.K / best_s);
     p.smem_bytes = qmv_smem(a, p.ks);
