@@ -41,18 +41,18 @@ namespace afb {
 namespace qmv {
 
 constexpr int GROUP = 64;
-constexpr int CW = 8;                            // consumer warps per CTA
 constexpr int XS_PAD = 8;
 
-// Rows per block (= TMA box height) and ring geometry for NT 16-row tiles per
-// consumer warp.
-template <int NT>
+// Ring geometry for CW consumer warps, each owning one 16-row tile of the
+// block: rows per block (= TMA box height), bytes per stage (packed words plus
+// the 8-group boxes of scales and biases) and the number of stages (~120 KB).
+template <int CW>
 struct Ring {
-    static constexpr int ROWS = 128 * NT;
-    static constexpr int W_BYTES = ROWS * 128;   // packed bytes per stage
-    static constexpr int SB_BYTES = ROWS * 16;   // one 8-group box of scales (or biases)
+    static constexpr int ROWS = 16 * CW;
+    static constexpr int W_BYTES = ROWS * 128;
+    static constexpr int SB_BYTES = ROWS * 16;
     static constexpr int STAGE_BYTES = W_BYTES + 2 * SB_BYTES;
-    static constexpr int STAGES = NT == 1 ? 6 : 3;
+    static constexpr int STAGES = (120 * 1024) / STAGE_BYTES;
 };
 
 struct Params {
@@ -120,13 +120,16 @@ __device__ __forceinline__ void tile_epilogue(const Params &p, const float (&acc
             const int64_t n = n0 + g + 8 * (i >> 1);
             if (m < p.M && n < p.N) p.partial[(static_cast<int64_t>(split) * p.M + m) * p.N + n] = acc[mt][i];
         }
-    __threadfence();
+    // Message passing through the arrival counter: release the partials with a
+    // gpu-scope acq_rel fence before the (relaxed) atomic; the last arriver
+    // fences again before reading the other splits' partials.
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     __syncwarp();
     unsigned prev = 0;
     if (lane == 0) prev = atomicAdd(&p.counters[tile], 1u);
     prev = __shfl_sync(0xffffffffu, prev, 0);
     if (prev != static_cast<unsigned>(p.splits - 1)) return;
-    __threadfence();
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -182,11 +185,12 @@ __device__ __forceinline__ void stage_x(const Params &p, char *xs, float *xg, in
     named_bar_sync(1, nthreads);
 }
 
-template <int BITS, int MT, int NT>
+template <int BITS, int MT, int CW>
 __global__ void __launch_bounds__(32 * (CW + 1), 1)
     qmv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const __grid_constant__ CUtensorMap bmap, Params p) {
-    using R = Ring<NT>;
+    constexpr int NT = 1;
+    using R = Ring<CW>;
     constexpr int STAGES = R::STAGES, STAGE_BYTES = R::STAGE_BYTES, W_BYTES = R::W_BYTES, SB_BYTES = R::SB_BYTES;
     constexpr int ROWS = R::ROWS;
     constexpr int GPS = Shape<BITS>::GPS;
@@ -407,9 +411,12 @@ bool qmv_supported(const QmmArgs &a, const char **why) {
 struct RingGeom {
     int rows, stages, stage_bytes;
 };
+// M <= 8: 16 consumer warps (256-row blocks); M > 8: 12 (192-row blocks),
+// bounded by the registers of the two-column-tile MMA variant.
+constexpr int kCwSmallM = 16, kCwLargeM = 12;
 static RingGeom ring_geom(const QmmArgs &a) {
-    if (a.M > 8) return {qmv::Ring<2>::ROWS, qmv::Ring<2>::STAGES, qmv::Ring<2>::STAGE_BYTES};
-    return {qmv::Ring<1>::ROWS, qmv::Ring<1>::STAGES, qmv::Ring<1>::STAGE_BYTES};
+    if (a.M > 8) return {qmv::Ring<kCwLargeM>::ROWS, qmv::Ring<kCwLargeM>::STAGES, qmv::Ring<kCwLargeM>::STAGE_BYTES};
+    return {qmv::Ring<kCwSmallM>::ROWS, qmv::Ring<kCwSmallM>::STAGES, qmv::Ring<kCwSmallM>::STAGE_BYTES};
 }
 
 static int qmv_smem(const QmmArgs &a, int ks) {
@@ -453,13 +460,13 @@ size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p) {
     return kPartialOffset + static_cast<size_t>(p.splits) * a.M * a.N * 4;
 }
 
-template <int BITS, int MT, int NT>
+template <int BITS, int MT, int CW>
 static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, const CUtensorMap &bm,
                               const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream) {
-    auto kern = qmv::qmv_kernel<BITS, MT, NT>;
+    auto kern = qmv::qmv_kernel<BITS, MT, CW>;
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(kern), plan.smem_bytes);
     if (e != cudaSuccess) return e;
-    kern<<<plan.grid_n, 32 * (qmv::CW + 1), plan.smem_bytes, stream>>>(wm, sm, bm, p);
+    kern<<<plan.grid_n, 32 * (CW + 1), plan.smem_bytes, stream>>>(wm, sm, bm, p);
     count_launch();
     return cudaGetLastError();
 }
@@ -495,8 +502,10 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
         return cudaErrorInvalidValue;
     const bool mt2 = a.M > 8;
     if (a.bits == 4)
-        return mt2 ? launch_cfg<4, 2, 2>(*wm, *sm, *bm, p, plan, stream) : launch_cfg<4, 1, 1>(*wm, *sm, *bm, p, plan, stream);
-    return mt2 ? launch_cfg<8, 2, 2>(*wm, *sm, *bm, p, plan, stream) : launch_cfg<8, 1, 1>(*wm, *sm, *bm, p, plan, stream);
+        return mt2 ? launch_cfg<4, 2, kCwLargeM>(*wm, *sm, *bm, p, plan, stream)
+                   : launch_cfg<4, 1, kCwSmallM>(*wm, *sm, *bm, p, plan, stream);
+    return mt2 ? launch_cfg<8, 2, kCwLargeM>(*wm, *sm, *bm, p, plan, stream)
+               : launch_cfg<8, 1, kCwSmallM>(*wm, *sm, *bm, p, plan, stream);
 }
 
 }  // namespace afb
