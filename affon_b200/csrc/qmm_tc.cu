@@ -16,7 +16,9 @@
 //   warp 2      TMA producer of packed-weight tiles
 //   warps 3-6   dequantisers: packed words -> bf16 w = fma(q, s, b) in the
 //               UMMA K-major 128-byte-swizzle layout, then
-//               fence.proxy.async so the tensor core sees the writes
+//               fence.proxy.async so the tensor core sees the writes; the
+//               packed stage is released (after another proxy fence) only
+//               once its words were decoded
 //   warps 7-10  epilogue: tcgen05.ld of the accumulator, f32/bf16 stores
 // Every wait is bounded (4 s); a timed-out wait sets the device status word
 // and lets all roles run to the end so TMEM is always released.
@@ -218,7 +220,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t bw = (gi < 2 ? bc.x : gi < 4 ? bc.y : gi < 6 ? bc.z : bc.w);
                 const uint32_t s2 = (gi & 1) ? ((sw >> 16) | (sw & 0xFFFF0000u)) : ((sw & 0xFFFFu) | (sw << 16));
                 const uint32_t b2 = (gi & 1) ? ((bw >> 16) | (bw & 0xFFFF0000u)) : ((bw & 0xFFFFu) | (bw << 16));
-                // packed words of this row for K block kb
+                mbar_wait(&sempty[s], ph ^ 1, abort, p.status);
                 mbar_wait(&pfull[ps_i], pph, abort, p.status);
                 const char *prow = ps + ps_i * C::P_BYTES + i * C::P_ROW;
                 uint32_t wv[BK * BITS / 32];
@@ -227,10 +229,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint4 q = *reinterpret_cast<const uint4 *>(prow + 16 * v);
                     wv[4 * v] = q.x; wv[4 * v + 1] = q.y; wv[4 * v + 2] = q.z; wv[4 * v + 3] = q.w;
                 }
-                mbar_arrive(&pempty[ps_i]);
-                if (++ps_i == PS) { ps_i = 0; pph ^= 1; }
-                // wait for the MMA to release this A stage, then write it
-                mbar_wait(&sempty[s], ph ^ 1, abort, p.status);
                 char *arow = as + s * A_BYTES + i * 128;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {  // 16-byte chunk j holds K = 8j..8j+7
@@ -247,6 +245,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int e = 0; e < 4; ++e) o[e] = bf16x2_fma(o[e], s2, b2);
                     *reinterpret_cast<uint4 *>(arow + ((j ^ (i & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
+                // Release the packed stage only after its words were consumed,
+                // with a proxy fence: the next TMA write (async proxy) must be
+                // ordered after these generic-proxy reads.
+                fence_proxy_async_smem();
+                mbar_arrive(&pempty[ps_i]);
+                if (++ps_i == PS) { ps_i = 0; pph ^= 1; }
                 fence_proxy_async_smem();
                 mbar_arrive(&afull[s]);
                 if (++s == S) { s = 0; ph ^= 1; }

@@ -377,6 +377,9 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
                     }
                 }
             }
+            // The stage is refilled by TMA (async proxy) after this release;
+            // order this warp's generic-proxy reads of it first.
+            fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);
             if (++stage == STAGES) { stage = 0; phase ^= 1; }
