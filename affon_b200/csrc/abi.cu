@@ -181,8 +181,8 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
     if (qmv_plannable && a.M <= 16) {
         c.impl = IMPL_QMV;
         c.plan = qplan;
-        snprintf(reason, sizeof reason, "M=%lld <= 16: decode qmv, split-K %d, %d CTAs per split", (long long)a.M,
-                 c.plan.splits, c.plan.grid_n);
+        snprintf(reason, sizeof reason, "M=%lld <= 16: decode qmv, stream-K over %d CTAs, %d K splits, %d-stage ring",
+                 (long long)a.M, c.plan.grid_n, c.plan.splits, c.plan.stages);
     } else if (tc_ok && (d->numerical_policy == AFFON_B200_POLICY_APPROXIMATE || a.y_bf16)) {
         c.impl = IMPL_QMM_TC;
         snprintf(reason, sizeof reason, "M=%lld >= 64: tcgen05 qmm with bf16-rounded decoded weights", (long long)a.M);

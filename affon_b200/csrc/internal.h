@@ -28,9 +28,11 @@ cudaError_t launch_qmm_generic(const QmmArgs &a, cudaStream_t stream);
 
 // Decode qmv for M <= 16, bits in {4, 8}, group 64, bf16 x/s/b, dense rows.
 struct QmvPlan {
-    int splits;      // split-K factor (>= 1; 0 = not plannable)
+    int splits;      // K splits (>= 1; 0 = not plannable): x slices that fit shared memory
     int ks;          // K per split
     int grid_n;      // persistent CTAs
+    int stages;      // shared-memory ring depth
+    int max_slots;   // partial-sum slots per block in the workspace
     int smem_bytes;
 };
 

@@ -3,33 +3,39 @@
 // activations / scales / biases, f32 accumulation (the layout and formula of
 // docs/core/quantized-inference.md:45-67).
 //
-// Streaming: a persistent CTA per SM.  One producer warp moves the packed
-// weight matrix through a ring of shared-memory stages with 2D TMA loads
-// (128 rows x 128 bytes per stage, 128-byte swizzle, plus the matching
-// 128 x 8 boxes of bf16 scales and biases; 256-row stages when M > 8), so
-// 120-160 KB per SM are in flight without costing registers.  Consumer warps read the packed
-// words from shared memory, decode them in registers and feed tensor cores.
+// Streaming.  Persistent CTAs, one per SM.  One producer warp moves the
+// packed weight matrix through a ring of shared-memory stages with 2D TMA
+// loads (ROWS rows x 128 bytes per stage, 128-byte swizzle, plus the matching
+// ROWS x 8 boxes of bf16 scales and biases), so ~120 KB per SM are in flight
+// without costing registers.  Consumer warps read the packed words from
+// shared memory, decode them in registers and feed tensor cores.
 //
 // Why tensor cores at M <= 16: at ~6.5 TB/s a 4-bit weight stream delivers
 // ~11.6e12 weights/s; decoding each weight to a float and multiplying it on
 // the CUDA cores costs ~3 lane-ops, as much as the 148 SMs can issue.  The
 // decoded codes go straight from registers into the A fragments of
 // m16n8k16 bf16 MMAs (weights as the 16-row A operand, activations as B).
+// Shifts of the nibble decoder are issued as mul.hi so they run on the FMA
+// pipe beside the logic ops on the ALU pipe.
 //
-// Exact codes, per-group affine in f32: the MMA multiplies the *integer codes*
-// q (exact in bf16) by x, giving C_g = sum_{k in g} x*q in f32; the affine
-// decode is applied per group of 64 outside the tensor core:
-//     y += s[n,g] * C_g + b[n,g] * X_g,   X_g = sum_{k in g} x[k]   (f32)
-// which is sum_k x*(s*q+b) up to reassociation; weights are never rounded to
-// bf16 (quantized-inference.md:119-121).  Numerical class: reassociated.
+// Exact codes, per-group affine in f32: the MMA multiplies the integer codes
+// (4-bit: as 128+q, exact in bf16) by x, giving C_g = sum_{k in g} x*code in
+// f32; the affine decode is applied per group of 64 outside the tensor core:
+//     y += s[n,g] * C_g + (b[n,g] - 128 s[n,g]) * X_g,  X_g = sum_{k in g} x[k]
+// evaluated as fused multiply-adds so the offset terms cancel exactly.  This
+// is sum_k x*(s*q+b) up to reassociation; weights are never rounded to bf16
+// (quantized-inference.md:119-121).  Numerical class: reassociated.
 //
-// Work units are (128-row block, K split).  A CTA takes a contiguous range of
-// units (split-major), stages its split's slice of x (4-bit: each 8-element
-// word permuted to match the nibble pairs the decoder produces) and the group
-// sums X_g in shared memory, then streams its blocks.  With splits > 1 each
-// warp writes f32 partials; the warp completing a tile last (per-tile arrival
-// counter in the workspace) sums them in split order, stores y and resets the
-// counter, so results do not depend on scheduling.
+// Work partition (stream-K).  The work is a flat list of items
+// (K split, 16*NT*CW-row block, 128-byte K stage), split-major.  CTA c takes
+// the items [c*T/C, (c+1)*T/C), so every CTA streams the same number of
+// bytes.  Splits exist only where x does not fit in shared memory; a CTA
+// restages x when its range enters a new split.  A block that lies inside one
+// CTA and one split is stored directly; a block shared by several CTAs or
+// splits is combined through f32 partials: each contributor writes its slot,
+// and the contributor arriving last (per-block counter) sums the slots in a
+// fixed order and stores y, so results do not depend on scheduling.  The
+// counter is reset by that last contributor for the next launch.
 #include <algorithm>
 #include <cmath>
 
@@ -42,17 +48,20 @@ namespace qmv {
 
 constexpr int GROUP = 64;
 constexpr int XS_PAD = 8;
+constexpr int MAX_STAGES = 8;
 
-// Ring geometry for CW consumer warps, each owning one 16-row tile of the
-// block: rows per block (= TMA box height), bytes per stage (packed words plus
-// the 8-group boxes of scales and biases) and the number of stages (~120 KB).
-template <int CW>
-struct Ring {
-    static constexpr int ROWS = 16 * CW;
-    static constexpr int W_BYTES = ROWS * 128;
-    static constexpr int SB_BYTES = ROWS * 16;
+template <int NT, int CW>
+struct Geom {
+    static constexpr int ROWS = 16 * NT * CW;   // rows per block (= TMA box height)
+    static constexpr int W_BYTES = ROWS * 128;  // packed bytes per stage
+    static constexpr int SB_BYTES = ROWS * 16;  // one 8-group box of scales (or biases)
     static constexpr int STAGE_BYTES = W_BYTES + 2 * SB_BYTES;
-    static constexpr int STAGES = (120 * 1024) / STAGE_BYTES;
+};
+
+template <int BITS>
+struct Shape {
+    static constexpr int GPS = BITS == 4 ? 4 : 2;  // groups per stage (128 packed bytes per row)
+    static constexpr int KPS = GPS * GROUP;         // K per stage
 };
 
 struct Params {
@@ -64,23 +73,22 @@ struct Params {
     unsigned *counters;
     unsigned *status;
     int M, N, K;
-    int splits, ks, nblocks, units;
+    int splits, ks;       // K splits (x slices that fit shared memory) and K per split
+    int nblocks, spb;     // blocks along N and stages per block per split
+    int64_t items;        // splits * nblocks * spb
+    int stages;           // ring depth
+    int max_slots;        // partial slots per block
     int y_bf16;
 };
 
-template <int BITS>
-struct Shape {
-    static constexpr int GPS = BITS == 4 ? 4 : 2;         // groups per stage (128 packed bytes per row)
-    static constexpr int KPS = GPS * GROUP;                // K per stage
-    static constexpr int WORDS_PER_STAGE = 32;             // u32 words per row per stage
-};
-
+__device__ __forceinline__ uint32_t shr_fma_pipe(uint32_t w, int s) {
+    uint32_t r;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(1u << (32 - s)));
+    return r;
+}
 // Codes p and p+4 of a 4-bit word as the exact bf16 pair (128+q_p, 128+q_{p+4}).
-// The +128 offset is removed per group in f32: s*(C' - 128*X_g) + b*X_g =
-// s*C' + (b - 128*s)*X_g, evaluated inside one fma so the large terms cancel
-// exactly and only C' (the tensor-core sum) carries rounding.
 __device__ __forceinline__ uint32_t dec4(uint32_t w, int p) {
-    return lop3_and_or(p ? (w >> (4 * p)) : w, 0x000F000Fu, 0x43004300u);
+    return lop3_and_or(p ? shr_fma_pipe(w, 4 * p) : w, 0x000F000Fu, 0x43004300u);
 }
 // Bytes i and i+1 of an 8-bit word as an exact bf16 pair (via 2^23 + q in f32).
 __device__ __forceinline__ uint32_t dec8(uint32_t w, int i) {
@@ -96,55 +104,86 @@ __device__ __forceinline__ void store_out(const Params &p, int m, int64_t n, flo
         static_cast<float *>(p.y)[m * p.ldy + n] = v;
 }
 
+// Owner CTA of flat item i when CTA c holds [floor(c*T/C), floor((c+1)*T/C)).
+__device__ __forceinline__ int owner_of(int64_t i, int64_t T, int C) {
+    return static_cast<int>(((i + 1) * C - 1) / T);
+}
+
+// Contributor count of block blk (all splits) and the slot of CTA c for split.
+__device__ __forceinline__ void contributors(const Params &p, int split, int blk, int c, int C, int &total,
+                                             int &slot) {
+    total = 0;
+    slot = -1;
+    for (int s = 0; s < p.splits; ++s) {
+        const int64_t b0 = (static_cast<int64_t>(s) * p.nblocks + blk) * p.spb;
+        const int first = owner_of(b0, p.items, C), last = owner_of(b0 + p.spb - 1, p.items, C);
+        if (s == split) slot = total + (c - first);
+        total += last - first + 1;
+    }
+}
+
+// Final values of one thread: rows n0+g and n0+g+8, activation rows 2t, 2t+1
+// (+8 for the second MMA column tile).
 template <int MT>
-__device__ __forceinline__ void tile_epilogue(const Params &p, const float (&acc)[MT][4], int tile, int split, int g,
-                                              int t, int lane) {
-    const int64_t n0 = static_cast<int64_t>(tile) * 16;
-    if (n0 >= p.N) return;
-    if (p.splits == 1) {
+__device__ __forceinline__ void store_tile(const Params &p, const float (&v)[MT][4], int64_t n0, int g, int t) {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int m = 2 * t + 8 * mt + (i & 1);
+            const int64_t n = n0 + g + 8 * (i >> 1);
+            if (m < p.M && n < p.N) store_out(p, m, n, v[mt][i]);
+        }
+}
+
+// Epilogue of one (split, block) segment of this CTA for the warp's NT tiles.
+template <int MT, int NT, int CW>
+__device__ __forceinline__ void segment_epilogue(const Params &p, float (&acc)[NT][MT][4], int split, int blk, int warp,
+                                                 int g, int t, int lane) {
+    constexpr int ROWS = Geom<NT, CW>::ROWS;
+    int total, slot;
+    contributors(p, split, blk, blockIdx.x, gridDim.x, total, slot);
+    const int64_t nb0 = static_cast<int64_t>(blk) * ROWS;
+    if (total == 1) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) store_tile<MT>(p, acc[nt], nb0 + (warp * NT + nt) * 16, g, t);
+        return;
+    }
+    // partial[((blk * max_slots + slot) * M + m) * ROWS + row]
+    float *base = p.partial + (static_cast<int64_t>(blk) * p.max_slots) * p.M * ROWS;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int m = 2 * t + 8 * mt + (i & 1);
-                const int64_t n = n0 + g + 8 * (i >> 1);
-                if (m < p.M && n < p.N) store_out(p, m, n, acc[mt][i]);
+                const int r = (warp * NT + nt) * 16 + g + 8 * (i >> 1);
+                if (m < p.M) base[(static_cast<int64_t>(slot) * p.M + m) * ROWS + r] = acc[nt][mt][i];
             }
-        return;
-    }
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int m = 2 * t + 8 * mt + (i & 1);
-            const int64_t n = n0 + g + 8 * (i >> 1);
-            if (m < p.M && n < p.N) p.partial[(static_cast<int64_t>(split) * p.M + m) * p.N + n] = acc[mt][i];
-        }
-    // Message passing through the arrival counter: release the partials with a
-    // gpu-scope acq_rel fence before the (relaxed) atomic; the last arriver
-    // fences again before reading the other splits' partials.
+    // Message passing through the per-block counter: release the partials
+    // with a gpu-scope acq_rel fence before the atomic; the last arriver
+    // fences again before reading every slot.  One arrival per warp, so the
+    // target is total * CW.
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
     __syncwarp();
     unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(&p.counters[tile], 1u);
+    if (lane == 0) prev = atomicAdd(&p.counters[blk], 1u);
     prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != static_cast<unsigned>(p.splits - 1)) return;
+    if (prev != static_cast<unsigned>(total * CW - 1)) return;
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int m = 2 * t + 8 * mt + (i & 1);
-            const int64_t n = n0 + g + 8 * (i >> 1);
-            if (m < p.M && n < p.N) {
-                float sum = 0.0f;
-                for (int sp = 0; sp < p.splits; ++sp)
-                    sum += __ldcg(&p.partial[(static_cast<int64_t>(sp) * p.M + m) * p.N + n]);
-                store_out(p, m, n, sum);
-            }
+    // This warp arrived last for the block: it reduces all rows of the block.
+    for (int r = lane; r < ROWS; r += 32) {
+        const int64_t n = nb0 + r;
+        if (n >= p.N) continue;
+        for (int m = 0; m < p.M; ++m) {
+            float sum = 0.0f;
+            for (int sl = 0; sl < total; ++sl) sum += __ldcg(&base[(static_cast<int64_t>(sl) * p.M + m) * ROWS + r]);
+            store_out(p, m, n, sum);
         }
+    }
     __syncwarp();
-    if (lane == 0) atomicExch(&p.counters[tile], 0u);
+    if (lane == 0) atomicExch(&p.counters[blk], 0u);
 }
 
 // Stage x[:, k0:k0+ks) (and the group sums X_g) into shared memory; run by
@@ -170,7 +209,7 @@ __device__ __forceinline__ void stage_x(const Params &p, char *xs, float *xg, in
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         sum += __shfl_xor_sync(0xffffffffu, sum, 4);
         if (valid) {
-            if constexpr (BITS == 4) {
+            if constexpr (BITS == 4) {  // [x0 x4 x1 x5 x2 x6 x3 x7] matches dec4's pairs
                 uint4 o;
                 o.x = prmt(v.x, v.z, 0x5410u);
                 o.y = prmt(v.x, v.z, 0x7632u);
@@ -185,28 +224,27 @@ __device__ __forceinline__ void stage_x(const Params &p, char *xs, float *xg, in
     named_bar_sync(1, nthreads);
 }
 
-template <int BITS, int MT, int CW>
+template <int BITS, int MT, int NT, int CW>
 __global__ void __launch_bounds__(32 * (CW + 1), 1)
     qmv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const __grid_constant__ CUtensorMap bmap, Params p) {
-    constexpr int NT = 1;
-    using R = Ring<CW>;
-    constexpr int STAGES = R::STAGES, STAGE_BYTES = R::STAGE_BYTES, W_BYTES = R::W_BYTES, SB_BYTES = R::SB_BYTES;
-    constexpr int ROWS = R::ROWS;
-    constexpr int GPS = Shape<BITS>::GPS;
+    using Gm = Geom<NT, CW>;
+    constexpr int STAGE_BYTES = Gm::STAGE_BYTES, W_BYTES = Gm::W_BYTES, SB_BYTES = Gm::SB_BYTES, ROWS = Gm::ROWS;
+    constexpr int GPS = Shape<BITS>::GPS, KPS = Shape<BITS>::KPS;
     extern __shared__ char smem_raw[];
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = p.stages;
     char *ring = smem;
     const int xs_rs = (p.ks + XS_PAD) * 2;
-    char *xs = ring + STAGES * STAGE_BYTES;
+    char *xs = ring + S * STAGE_BYTES;
     float *xg = reinterpret_cast<float *>(xs + p.M * xs_rs);
     uint64_t *full = reinterpret_cast<uint64_t *>(xg + (p.ks / GROUP) * 16);
-    uint64_t *empty = full + STAGES;
-    volatile int *abort = reinterpret_cast<volatile int *>(empty + STAGES);
+    uint64_t *empty = full + MAX_STAGES;
+    volatile int *abort = reinterpret_cast<volatile int *>(empty + MAX_STAGES);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CW);
         }
@@ -215,9 +253,10 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
     }
     __syncthreads();
 
-    const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.units / gridDim.x);
-    const int u_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.units / gridDim.x);
-    const int nst = p.ks / Shape<BITS>::KPS;  // stages per unit
+    const int64_t T = p.items;
+    const int64_t lo = static_cast<int64_t>(blockIdx.x) * T / gridDim.x;
+    const int64_t hi = static_cast<int64_t>(blockIdx.x + 1) * T / gridDim.x;
+    const int64_t per_split = static_cast<int64_t>(p.nblocks) * p.spb;
 
     if (warp == CW) {  // ------------------------------------------ producer
         if (lane == 0) {
@@ -226,21 +265,20 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
             tma_prefetch_desc(&bmap);
             int stage = 0;
             uint32_t phase = 0;
-            for (int u = u_begin; u < u_end; ++u) {
-                const int split = u / p.nblocks, blk = u - split * p.nblocks;
-                const int64_t k0 = static_cast<int64_t>(split) * p.ks;
-                for (int j = 0; j < nst; ++j) {
-                    // On a timed-out wait (abort set) stop issuing loads; consumers drain.
-                    if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) return;
-                    char *dst = ring + stage * STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                    const int64_t kk = k0 + static_cast<int64_t>(j) * Shape<BITS>::KPS;
-                    tma_load_2d(dst, &wmap, &full[stage], static_cast<int>(kk * BITS / 32), blk * ROWS);
-                    const int g8 = static_cast<int>((kk / GROUP) & ~int64_t(7));
-                    tma_load_2d(dst + W_BYTES, &smap, &full[stage], g8, blk * ROWS);
-                    tma_load_2d(dst + W_BYTES + SB_BYTES, &bmap, &full[stage], g8, blk * ROWS);
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
-                }
+            for (int64_t i = lo; i < hi; ++i) {
+                const int split = static_cast<int>(i / per_split);
+                const int64_t rem = i - split * per_split;
+                const int blk = static_cast<int>(rem / p.spb), st = static_cast<int>(rem - int64_t(blk) * p.spb);
+                // On a timed-out wait (abort set) stop issuing loads; consumers drain.
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) return;
+                char *dst = ring + stage * STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                const int64_t kk = static_cast<int64_t>(split) * p.ks + static_cast<int64_t>(st) * KPS;
+                tma_load_2d(dst, &wmap, &full[stage], static_cast<int>(kk * BITS / 32), blk * ROWS);
+                const int g8 = static_cast<int>((kk / GROUP) & ~int64_t(7));
+                tma_load_2d(dst + W_BYTES, &smap, &full[stage], g8, blk * ROWS);
+                tma_load_2d(dst + W_BYTES + SB_BYTES, &bmap, &full[stage], g8, blk * ROWS);
+                if (++stage == S) { stage = 0; phase ^= 1; }
             }
         }
         return;
@@ -251,8 +289,13 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
     int stage = 0;
     uint32_t phase = 0;
     int cur_split = -1;
-    for (int u = u_begin; u < u_end; ++u) {
-        const int split = u / p.nblocks, blk = u - split * p.nblocks;
+    int64_t i = lo;
+    while (i < hi) {
+        const int split = static_cast<int>(i / per_split);
+        const int64_t rem = i - split * per_split;
+        const int blk = static_cast<int>(rem / p.spb);
+        const int64_t blk_begin = static_cast<int64_t>(split) * per_split + static_cast<int64_t>(blk) * p.spb;
+        const int64_t seg_end = min(hi, blk_begin + p.spb);
         if (split != cur_split) {
             named_bar_sync(1, CW * 32);
             stage_x<BITS>(p, xs, xg, xs_rs, static_cast<int64_t>(split) * p.ks, tid, CW * 32);
@@ -264,7 +307,8 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) acc[nt][mt][0] = acc[nt][mt][1] = acc[nt][mt][2] = acc[nt][mt][3] = 0.f;
 
-        for (int j = 0; j < nst; ++j) {
+        for (; i < seg_end; ++i) {
+            const int j = static_cast<int>(i - blk_begin);  // stage index within the block
             // A timed-out wait sets *abort; keep walking the loop (results are
             // then garbage and the status word says TIMEOUT) so that every
             // consumer reaches the same named barriers and no thread hangs.
@@ -273,8 +317,6 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
             const char *ssb = sw + W_BYTES;
             const char *bsb = ssb + SB_BYTES;
             const int go0 = (j * GPS) & 7;  // first group of this stage within the 8-group scale box
-            // Scales and biases of this stage for rows r0 and r0+8 of each tile:
-            // GPS bf16 per row (8 bytes for 4-bit, 4 bytes for 8-bit).
             uint32_t sv[NT][2][GPS / 2], bv[NT][2][GPS / 2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
@@ -292,7 +334,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
                 }
 #pragma unroll
             for (int G = 0; G < GPS; ++G) {
-                const int Gl = j * GPS + G;           // group index within the split
+                const int Gl = j * GPS + G;  // group index within the split
                 uint32_t xf[MT][8];
                 float2 X[MT];
 #pragma unroll
@@ -306,7 +348,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
                         xf[mt][4] = v1.x; xf[mt][5] = v1.y; xf[mt][6] = v1.z; xf[mt][7] = v1.w;
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) xf[mt][i] = 0u;
+                        for (int e = 0; e < 8; ++e) xf[mt][e] = 0u;
                     }
                     X[mt] = *reinterpret_cast<const float2 *>(xg + Gl * 16 + 2 * t + 8 * mt);
                 }
@@ -382,11 +424,9 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[stage]);
-            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            if (++stage == S) { stage = 0; phase ^= 1; }
         }
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-            tile_epilogue<MT>(p, acc[nt], blk * (ROWS / 16) + warp * NT + nt, split, g, t, lane);
+        segment_epilogue<MT, NT, CW>(p, acc, split, blk, warp, g, t, lane);
     }
 }
 
@@ -406,67 +446,80 @@ bool qmv_supported(const QmmArgs &a, const char **why) {
     if (!al(a.w.ptr, 16) || (a.w.row_stride * 4) % 16) return no("qmv: packed rows must be 16-byte aligned");
     if (!al(a.s.ptr, 16) || !al(a.b.ptr, 16) || (a.s.row_stride * 2) % 16 || (a.b.row_stride * 2) % 16)
         return no("qmv: parameter rows must be 16-byte aligned");
-    if ((a.N + 15) / 16 > kMaxTiles) return no("qmv: N beyond the arrival-counter region");
+    if ((a.N + 255) / 256 > kMaxTiles) return no("qmv: N beyond the arrival-counter region");
     if (a.N >= (int64_t(1) << 31) || a.K >= (int64_t(1) << 30)) return no("qmv: size beyond 32-bit indexing");
     return true;
 }
 
-struct RingGeom {
-    int rows, stages, stage_bytes;
+namespace {
+
+// M <= 8: one column tile, 16 consumer warps of one 16-row tile each
+// (256-row blocks).  M > 8: two column tiles; 8 consumer warps of two 16-row
+// tiles each (256-row blocks) so each activation fragment feeds two tiles.
+struct Variant {
+    int nt, cw, rows, stage_bytes;
 };
-// M <= 8: 16 consumer warps (256-row blocks); M > 8: 12 (192-row blocks),
-// bounded by the registers of the two-column-tile MMA variant.
-constexpr int kCwSmallM = 16, kCwLargeM = 12;
-static RingGeom ring_geom(const QmmArgs &a) {
-    if (a.M > 8) return {qmv::Ring<kCwLargeM>::ROWS, qmv::Ring<kCwLargeM>::STAGES, qmv::Ring<kCwLargeM>::STAGE_BYTES};
-    return {qmv::Ring<kCwSmallM>::ROWS, qmv::Ring<kCwSmallM>::STAGES, qmv::Ring<kCwSmallM>::STAGE_BYTES};
+Variant variant_of(const QmmArgs &a) {
+    if (a.M > 8) return {2, 8, qmv::Geom<2, 8>::ROWS, qmv::Geom<2, 8>::STAGE_BYTES};
+    return {1, 16, qmv::Geom<1, 16>::ROWS, qmv::Geom<1, 16>::STAGE_BYTES};
 }
 
-static int qmv_smem(const QmmArgs &a, int ks) {
-    const RingGeom r = ring_geom(a);
-    return 1024 + r.stages * r.stage_bytes + static_cast<int>(a.M) * (ks + qmv::XS_PAD) * 2 + (ks / 64) * 16 * 4 +
-           2 * r.stages * 8 + 16;
-}
+int x_bytes(const QmmArgs &a, int ks) { return static_cast<int>(a.M) * (ks + qmv::XS_PAD) * 2 + (ks / 64) * 16 * 4; }
+
+constexpr int kSmemCap = 227 * 1024;
+constexpr int kMinRing = 2 * 40 * 1024;   // keep >= 80 KB of weights in flight
+constexpr int kMaxRing = 128 * 1024;
+
+}  // namespace
 
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
-    const int nk = static_cast<int>(a.K / 512);
-    const int64_t nblocks = (a.N + ring_geom(a).rows - 1) / ring_geom(a).rows;
-    const int smem_cap = 227 * 1024;
-    auto ws_ok = [&](int s) {
-        return s == 1 || kPartialOffset + static_cast<size_t>(s) * a.M * a.N * 4 <= workspace_bytes;
-    };
-    int smin = 0;
-    for (int s = 1; s <= nk; ++s)
-        if (nk % s == 0 && qmv_smem(a, static_cast<int>(a.K / s)) <= smem_cap) { smin = s; break; }
     QmvPlan p{};
-    if (smin == 0) return p;  // splits == 0: not plannable
-    double best = -1.0;
-    int best_s = 0;
-    for (int s = smin; s <= nk; ++s) {
-        if (nk % s || !ws_ok(s)) continue;
-        const int64_t units = nblocks * s;
-        const int64_t waves = (units + num_sms - 1) / num_sms;
-        const double eff = static_cast<double>(units) / static_cast<double>(waves * num_sms);
-        const double score = eff * (1.0 - 0.03 * std::log2(static_cast<double>(s) / smin));
-        if (score > best + 1e-9) { best = score; best_s = s; }
+    const Variant v = variant_of(a);
+    const int nk = static_cast<int>(a.K / 512);
+    const int overhead = 1024 + 2 * qmv::MAX_STAGES * 8 + 64;
+    int splits = 0;
+    for (int s = 1; s <= nk; ++s) {
+        if (nk % s) continue;
+        if (overhead + x_bytes(a, static_cast<int>(a.K / s)) + std::max(kMinRing, 2 * v.stage_bytes) <= kSmemCap) {
+            splits = s;
+            break;
+        }
     }
-    if (best_s == 0) return p;  // no split fits the workspace: not plannable
-    p.splits = best_s;
-    p.ks = static_cast<int>(a.K / best_s);
-    p.smem_bytes = qmv_smem(a, p.ks);
-    p.grid_n = static_cast<int>(std::min<int64_t>(num_sms, nblocks * best_s));
+    if (splits == 0) return p;
+    const int ks = static_cast<int>(a.K / splits);
+    const int ring_room = kSmemCap - overhead - x_bytes(a, ks);
+    const int stages = std::min(qmv::MAX_STAGES, std::min(ring_room, kMaxRing) / v.stage_bytes);
+    if (stages < 2) return p;
+    const int64_t nblocks = (a.N + v.rows - 1) / v.rows;
+    const int kps = a.bits == 4 ? 256 : 128;
+    const int64_t spb = ks / kps;
+    const int64_t items = nblocks * spb * splits;
+    const int grid = static_cast<int>(std::min<int64_t>(num_sms, items));
+    // Upper bound of contributors per block: per split, a block spans at most
+    // ceil(spb / floor(items/grid)) + 1 CTAs.
+    const int64_t per_cta = std::max<int64_t>(1, items / grid);
+    const int max_slots = static_cast<int>(splits * ((spb + per_cta - 1) / per_cta + 1));
+    const size_t need = kPartialOffset + static_cast<size_t>(nblocks) * max_slots * a.M * v.rows * 4;
+    if (need > workspace_bytes) return p;
+    p.splits = splits;
+    p.ks = ks;
+    p.grid_n = grid;
+    p.stages = stages;
+    p.max_slots = max_slots;
+    p.smem_bytes = overhead + x_bytes(a, ks) + stages * v.stage_bytes;
     return p;
 }
 
 size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p) {
-    if (p.splits <= 1) return 0;
-    return kPartialOffset + static_cast<size_t>(p.splits) * a.M * a.N * 4;
+    const Variant v = variant_of(a);
+    const int64_t nblocks = (a.N + v.rows - 1) / v.rows;
+    return kPartialOffset + static_cast<size_t>(nblocks) * p.max_slots * a.M * v.rows * 4;
 }
 
-template <int BITS, int MT, int CW>
+template <int BITS, int MT, int NT, int CW>
 static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, const CUtensorMap &bm,
                               const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream) {
-    auto kern = qmv::qmv_kernel<BITS, MT, CW>;
+    auto kern = qmv::qmv_kernel<BITS, MT, NT, CW>;
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(kern), plan.smem_bytes);
     if (e != cudaSuccess) return e;
     kern<<<plan.grid_n, 32 * (CW + 1), plan.smem_bytes, stream>>>(wm, sm, bm, p);
@@ -476,7 +529,7 @@ static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, cons
 
 cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, cudaStream_t stream) {
     if (plan.splits < 1) return cudaErrorInvalidValue;
-    const int rows = ring_geom(a).rows;
+    const Variant v = variant_of(a);
     qmv::Params p{};
     p.x = static_cast<const uint16_t *>(a.x.ptr);
     p.ldx = a.x.row_stride;
@@ -487,8 +540,11 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     p.K = static_cast<int>(a.K);
     p.splits = plan.splits;
     p.ks = plan.ks;
-    p.nblocks = static_cast<int>((a.N + rows - 1) / rows);
-    p.units = p.nblocks * p.splits;
+    p.nblocks = static_cast<int>((a.N + v.rows - 1) / v.rows);
+    p.spb = plan.ks / (a.bits == 4 ? 256 : 128);
+    p.items = static_cast<int64_t>(p.nblocks) * p.spb * p.splits;
+    p.stages = plan.stages;
+    p.max_slots = plan.max_slots;
     p.y_bf16 = a.y_bf16;
     char *ws = static_cast<char *>(workspace);
     p.status = reinterpret_cast<unsigned *>(ws);
@@ -496,19 +552,18 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     p.partial = reinterpret_cast<float *>(ws + kPartialOffset);
     const CUtensorMap *wm, *sm, *bm;
     const uint64_t words = static_cast<uint64_t>(a.K) * a.bits / 32;
-    if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32, rows,
+    if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32, v.rows,
                                     CU_TENSOR_MAP_SWIZZLE_128B)) ||
         !(sm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2, 8,
-                                    rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+                                    v.rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
         !(bm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2, 8,
-                                    rows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+                                    v.rows, CU_TENSOR_MAP_SWIZZLE_NONE)))
         return cudaErrorInvalidValue;
-    const bool mt2 = a.M > 8;
-    if (a.bits == 4)
-        return mt2 ? launch_cfg<4, 2, kCwLargeM>(*wm, *sm, *bm, p, plan, stream)
-                   : launch_cfg<4, 1, kCwSmallM>(*wm, *sm, *bm, p, plan, stream);
-    return mt2 ? launch_cfg<8, 2, kCwLargeM>(*wm, *sm, *bm, p, plan, stream)
-               : launch_cfg<8, 1, kCwSmallM>(*wm, *sm, *bm, p, plan, stream);
+    if (a.M > 8)
+        return a.bits == 4 ? launch_cfg<4, 2, 2, 8>(*wm, *sm, *bm, p, plan, stream)
+                           : launch_cfg<8, 2, 2, 8>(*wm, *sm, *bm, p, plan, stream);
+    return a.bits == 4 ? launch_cfg<4, 1, 1, 16>(*wm, *sm, *bm, p, plan, stream)
+                       : launch_cfg<8, 1, 1, 16>(*wm, *sm, *bm, p, plan, stream);
 }
 
 }  // namespace afb

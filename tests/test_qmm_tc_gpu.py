@@ -102,3 +102,22 @@ def test_qmm_tc_large_property(ctx):
     want = xs @ wsum
     got = y[:4].sum(axis=1)
     assert np.abs(got - want).max() <= 2e-2 * np.abs(y[:4]).sum(axis=1).max() / np.sqrt(N) + 1e-3 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_qmm_tc_repeated_runs_are_identical_and_bounded(ctx, bits):
+    """Pipeline-race guard: a multi-tile shape (more tiles than SMs) run five
+    times must give bit-identical results, every element within the
+    single-rounding bound of the float64 contraction."""
+    M, N, K = 512, 14336, 4096
+    data = synthetic.quantized_linear(M, N, K, bits=bits, seed=2)
+    ref, mag = _f64(data)
+    first = None
+    for _ in range(5):
+        y, impl = _run(ctx, data, "f32", "approximate")
+        assert "qmm_tcgen05" in impl
+        assert (np.abs(y - ref) <= 2.0 ** -8 * mag + 1e-6).all()
+        if first is None:
+            first = y
+        else:
+            np.testing.assert_array_equal(y, first)
