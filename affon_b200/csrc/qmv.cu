@@ -29,13 +29,14 @@
 // Work partition (stream-K).  The work is a flat list of items
 // (K split, 16*NT*CW-row block, 128-byte K stage), split-major.  CTA c takes
 // the items [c*T/C, (c+1)*T/C), so every CTA streams the same number of
-// bytes.  Splits exist only where x does not fit in shared memory; a CTA
-// restages x when its range enters a new split.  A block that lies inside one
-// CTA and one split is stored directly; a block shared by several CTAs or
-// splits is combined through f32 partials: each contributor writes its slot,
-// and the contributor arriving last (per-block counter) sums the slots in a
-// fixed order and stores y, so results do not depend on scheduling.  The
-// counter is reset by that last contributor for the next launch.
+// bytes.  K is split where x would not fit in shared memory and, beyond that,
+// where staging x in every CTA would cost more on-chip traffic than the extra
+// partial sums; a CTA restages x when its range enters a new split.  A block
+// that lies inside one CTA and one split is stored directly; a block shared
+// by several CTAs or splits is combined through f32 partials: each
+// contributing CTA writes its slot, and the CTA arriving last (per-block
+// counter) sums the slots in a fixed order and stores y, so results do not
+// depend on scheduling.  That CTA resets the counter for the next launch.
 #include <algorithm>
 #include <cmath>
 
@@ -137,9 +138,10 @@ __device__ __forceinline__ void store_tile(const Params &p, const float (&v)[MT]
 }
 
 // Epilogue of one (split, block) segment of this CTA for the warp's NT tiles.
+// Called by all consumer warps together.  `flag` is a shared-memory word.
 template <int MT, int NT, int CW>
 __device__ __forceinline__ void segment_epilogue(const Params &p, float (&acc)[NT][MT][4], int split, int blk, int warp,
-                                                 int g, int t, int lane) {
+                                                 int g, int t, int lane, int tid, volatile int *flag) {
     constexpr int ROWS = Geom<NT, CW>::ROWS;
     int total, slot;
     contributors(p, split, blk, blockIdx.x, gridDim.x, total, slot);
@@ -161,19 +163,21 @@ __device__ __forceinline__ void segment_epilogue(const Params &p, float (&acc)[N
                 const int r = (warp * NT + nt) * 16 + g + 8 * (i >> 1);
                 if (m < p.M) base[(static_cast<int64_t>(slot) * p.M + m) * ROWS + r] = acc[nt][mt][i];
             }
-    // Message passing through the per-block counter: release the partials
-    // with a gpu-scope acq_rel fence before the atomic; the last arriver
-    // fences again before reading every slot.  One arrival per warp, so the
-    // target is total * CW.
+    // Message passing through the per-block counter (one arrival per
+    // contributing CTA): every thread releases its partials with a gpu-scope
+    // acq_rel fence, the consumer warps meet, one thread takes the ticket,
+    // and in the last contributor every thread fences again before reading
+    // all slots.
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    __syncwarp();
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(&p.counters[blk], 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != static_cast<unsigned>(total * CW - 1)) return;
+    named_bar_sync(1, CW * 32);
+    if (tid == 0) *flag = (atomicAdd(&p.counters[blk], 1u) == static_cast<unsigned>(total - 1)) ? 1 : 0;
+    named_bar_sync(1, CW * 32);
+    const bool last = *flag != 0;
+    named_bar_sync(1, CW * 32);  // the flag is reused by the next segment
+    if (!last) return;
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    // This warp arrived last for the block: it reduces all rows of the block.
-    for (int r = lane; r < ROWS; r += 32) {
+    // Each warp reduces the rows it owns: lanes over rows, so loads coalesce.
+    for (int r = warp * 16 * NT + lane; r < (warp + 1) * 16 * NT; r += 32) {
         const int64_t n = nb0 + r;
         if (n >= p.N) continue;
         for (int m = 0; m < p.M; ++m) {
@@ -182,8 +186,7 @@ __device__ __forceinline__ void segment_epilogue(const Params &p, float (&acc)[N
             store_out(p, m, n, sum);
         }
     }
-    __syncwarp();
-    if (lane == 0) atomicExch(&p.counters[blk], 0u);
+    if (tid == 0) atomicExch(&p.counters[blk], 0u);
 }
 
 // Stage x[:, k0:k0+ks) (and the group sums X_g) into shared memory; run by
@@ -241,6 +244,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(xg + (p.ks / GROUP) * 16);
     uint64_t *empty = full + MAX_STAGES;
     volatile int *abort = reinterpret_cast<volatile int *>(empty + MAX_STAGES);
+    volatile int *flag = abort + 1;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
@@ -426,7 +430,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
             if (lane == 0) mbar_arrive(&empty[stage]);
             if (++stage == S) { stage = 0; phase ^= 1; }
         }
-        segment_epilogue<MT, NT, CW>(p, acc, split, blk, warp, g, t, lane);
+        segment_epilogue<MT, NT, CW>(p, acc, split, blk, warp, g, t, lane, tid, flag);
     }
 }
 
@@ -477,15 +481,24 @@ QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     const Variant v = variant_of(a);
     const int nk = static_cast<int>(a.K / 512);
     const int overhead = 1024 + 2 * qmv::MAX_STAGES * 8 + 64;
-    int splits = 0;
+    // K splits: the smallest count whose x slice fits next to the ring, raised
+    // towards the count that balances the two on-chip costs of stream-K --
+    // every CTA stages its x slice (grid * M * K/S * 2 bytes) while every
+    // extra split adds partial sums (about 8 * S * M * N bytes) -- which is
+    // minimised near S = sqrt(grid * K / (4 * N)).
+    int smin = 0;
     for (int s = 1; s <= nk; ++s) {
         if (nk % s) continue;
         if (overhead + x_bytes(a, static_cast<int>(a.K / s)) + std::max(kMinRing, 2 * v.stage_bytes) <= kSmemCap) {
-            splits = s;
+            smin = s;
             break;
         }
     }
-    if (splits == 0) return p;
+    if (smin == 0) return p;
+    const double s_opt = std::sqrt(static_cast<double>(num_sms) * a.K / (4.0 * a.N));
+    int splits = smin;
+    for (int s = smin; s <= nk; ++s)
+        if (nk % s == 0 && s <= s_opt * 1.5) splits = s;
     const int ks = static_cast<int>(a.K / splits);
     const int ring_room = kSmemCap - overhead - x_bytes(a, ks);
     const int stages = std::min(qmv::MAX_STAGES, std::min(ring_room, kMaxRing) / v.stage_bytes);
