@@ -51,6 +51,7 @@ SIGNATURES = {
     "affon_b200_qmm_host": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
     "affon_b200_compute_core_run_quantized_matmul_f32": ([c_vp, c_sz, c_vp, c_sz, c_vp, c_sz, c_vp, c_sz, c_vp, c_sz,
                                                           c_sz, c_sz, c_sz, c_sz, c_sz], c_i32),
+    "affon_b200_qmv_noalloc": ([ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
     "affon_b200_launch_count": ([], ctypes.c_uint64),
 }
 

@@ -258,6 +258,18 @@ thread_local affon_b200_ctx *t_default_ctx = nullptr;
 
 }  // namespace
 
+// Shared with other translation units of the library (see internal.h).
+namespace afb {
+int validate_qmm_desc(const affon_b200_qmm_desc *d) { return validate_desc(d); }
+QmmArgs qmm_args_from_desc(const affon_b200_qmm_desc *d, const void *x, const void *w, const void *s, const void *b,
+                           void *y) {
+    return make_args(d, x, w, s, b, y);
+}
+int set_error(int status, const char *msg) { return fail(status, "%s", msg); }
+int set_cuda_error(cudaError_t e, const char *what) { return cuda_fail(e, what); }
+void clear_error() { t_error.clear(); }
+}  // namespace afb
+
 extern "C" {
 
 int affon_b200_abi_version(void) { return AFFON_B200_ABI_VERSION; }

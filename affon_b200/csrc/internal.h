@@ -54,3 +54,16 @@ cudaError_t launch_qmm_tc(const QmmArgs &a, void *workspace, cudaStream_t stream
 void count_launch(uint64_t n = 1);
 
 }  // namespace afb
+
+struct affon_b200_qmm_desc;
+namespace afb {
+// Descriptor validation, argument resolution and the thread-local error
+// message of the C ABI (abi.cu), for other entry points of the library.
+int validate_qmm_desc(const affon_b200_qmm_desc *d);
+QmmArgs qmm_args_from_desc(const affon_b200_qmm_desc *d, const void *x, const void *w, const void *s, const void *b,
+                           void *y);
+int set_error(int status, const char *msg);
+int set_cuda_error(cudaError_t e, const char *what);
+void clear_error();
+
+}  // namespace afb

@@ -164,6 +164,24 @@ int affon_b200_compute_core_run_quantized_matmul_f32(
     const float *scales, size_t scale_count, const float *biases, size_t bias_count, float *output,
     size_t output_count, size_t rows, size_t depth, size_t columns, size_t bits, size_t group_size);
 
+/* Decode qmv without any device allocation.  (No counterpart in the
+ * reference: an addition for callers that cannot let a library allocate
+ * device memory -- runtimes that own all GPU memory in a pre-reserved arena,
+ * plugin hosts whose allocator is the only one allowed to call the driver, or
+ * code running while a stream is being captured.)  Same contract and results
+ * as affon_b200_qmm for the decode qmv (M <= 16, 4/8-bit, group 64, bf16
+ * activations and parameters); other descriptors return
+ * AFFON_B200_UNSUPPORTED.  No context is needed: the launch goes to
+ * `cuda_stream` on the current device, and the kernel's scratch lives in a
+ * static 8 MiB device array that every GPU loading this library holds until
+ * exit; shapes whose partial sums exceed it (large M*N) are rejected with
+ * AFFON_B200_UNSUPPORTED and a message.  The first call on a device looks up
+ * that array's device address, so make it before any stream capture.  All
+ * calls share the one array: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller. */
+int affon_b200_qmv_noalloc(const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w, const void *s,
+                           const void *b, void *y, void *cuda_stream);
+
 /* Number of kernel launches this library issued in this process (all
  * contexts); lets callers and benchmarks count native launches. */
 uint64_t affon_b200_launch_count(void);

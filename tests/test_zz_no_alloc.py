@@ -1,0 +1,74 @@
+"""The allocation-free decode qmv entry point, affon_b200_qmv_noalloc.
+
+It exists for callers that may not allocate device memory through a library
+(an arena-owning runtime, a plugin host with its own allocator, code running
+under stream capture): it needs no context and keeps its scratch in a static
+device array.  These tests call it through the C ABI and compare it with the
+regular context-based entry point on the same inputs, twice in a row (the
+array keeps the previous call's contents, so the second call checks that
+what must start at zero is cleared).  The file sorts last so that a run
+stopping at the first failure has already run every other test.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from affon_b200 import _lib, synthetic
+from gpu_util import Ctx, dense_desc
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = Ctx(0)
+    yield c
+    c.close()
+
+
+def _upload(data, dev):
+    return {k: torch.from_numpy(np.ascontiguousarray(data[k]).view(np.int32 if data[k].dtype == np.uint32 else
+                                                                    np.int16)).to(dev) for k in ("x", "w", "s", "b")}
+
+
+@pytest.mark.parametrize("M,N,K,bits,yd", [(16, 4096, 4096, 4, "f32"), (1, 14336, 4096, 4, "bf16"),
+                                           (8, 4096, 14336, 8, "f32"), (4, 28672, 4096, 4, "f32")])
+def test_noalloc_matches_context_entry_twice(ctx, M, N, K, bits, yd):
+    data = synthetic.quantized_linear(M, N, K, bits=bits, seed=21)
+    dev = ctx.device
+    bufs = _upload(data, dev)
+    ptrs = [bufs[k].data_ptr() for k in ("x", "w", "s", "b")]
+    tdt = torch.float32 if yd == "f32" else torch.bfloat16
+    d = dense_desc(M, N, K, bits, yd=yd)
+
+    y_ref = torch.full((M, N), float("nan"), dtype=tdt, device=dev)
+    sel = ctx.qmm(d, *ptrs, y_ref.data_ptr())
+    assert "qmv" in sel.implementation_id.decode()
+    torch.cuda.synchronize()
+    ref = y_ref.float().cpu().numpy()
+    tol = (1e-5 if yd == "f32" else 2e-2) * max(1.0, float(np.abs(ref).max()))
+
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(2):
+        y = torch.full((M, N), float("nan"), dtype=tdt, device=dev)
+        rc = _lib.lib().affon_b200_qmv_noalloc(ctypes.byref(d), *ptrs, y.data_ptr(), stream)
+        assert rc == 0, _lib.last_error()
+        torch.cuda.synchronize()
+        got = y.float().cpu().numpy()
+        assert np.isfinite(got).all()
+        assert np.abs(got - ref).max() <= tol
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch(ctx):
+    """M*N beyond the static scratch is refused before any launch, with a message."""
+    M, N, K = 16, 128256, 4096
+    d = dense_desc(M, N, K, 4)
+    y = torch.zeros((M, N), dtype=torch.float32, device=ctx.device)
+    dummy = torch.zeros(16, dtype=torch.int32, device=ctx.device).data_ptr()
+    rc = _lib.lib().affon_b200_qmv_noalloc(ctypes.byref(d), dummy, dummy, dummy, dummy, y.data_ptr(),
+                                           torch.cuda.current_stream(ctx.device).cuda_stream)
+    assert rc == _lib.UNSUPPORTED
+    assert "scratch" in _lib.last_error()
+    assert (y == 0).all()
