@@ -28,6 +28,22 @@ class QmmDesc(ctypes.Structure):
                 ("reserved", c_i32), ("x", View), ("w", View), ("s", View), ("b", View), ("y", View)]
 
 
+class QmvFusion(ctypes.Structure):
+    _fields_ = [("struct_size", c_u32), ("x_mode", c_i32), ("h_in", c_vp), ("ld_h_in", c_i64), ("ss_in", c_vp),
+                ("ss_tiles", c_i32), ("eps", ctypes.c_float), ("gamma", c_vp), ("epilogue", c_i32),
+                ("reserved", c_i32), ("h_out", c_vp), ("ld_h_out", c_i64), ("ss_out", c_vp), ("act", c_vp),
+                ("ld_act", c_i64), ("amax", c_vp)]
+
+
+class AttnDesc(ctypes.Structure):
+    _fields_ = [("struct_size", c_u32), ("batch", c_i32), ("q_heads", c_i32), ("kv_heads", c_i32),
+                ("head_dim", c_i32), ("capacity", c_i32), ("scale", ctypes.c_float), ("q_offset", c_i32),
+                ("k_offset", c_i32), ("v_offset", c_i32), ("reserved", c_i32), ("ld_qkv", c_i64), ("ld_out", c_i64)]
+
+
+EPI_STORE, EPI_RESID, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
+
+
 class Selection(ctypes.Structure):
     _fields_ = [("implementation_id", ctypes.c_char * 64), ("implementation_version", c_i32),
                 ("numerical_class", c_i32), ("splits", c_i32), ("reserved", c_i32), ("reason", ctypes.c_char * 256)]
@@ -52,6 +68,11 @@ SIGNATURES = {
     "affon_b200_compute_core_run_quantized_matmul_f32": ([c_vp, c_sz, c_vp, c_sz, c_vp, c_sz, c_vp, c_sz, c_vp, c_sz,
                                                           c_sz, c_sz, c_sz, c_sz, c_sz], c_i32),
     "affon_b200_qmv_noalloc": ([ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_qmv_fused": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp,
+                              ctypes.POINTER(QmvFusion)], c_i32),
+    "affon_b200_decode_attention": ([c_vp, ctypes.POINTER(AttnDesc), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_embed": ([c_vp, c_vp, c_i64, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_argmax_finalize": ([c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp], c_i32),
     "affon_b200_launch_count": ([], ctypes.c_uint64),
 }
 

@@ -439,6 +439,117 @@ int affon_b200_qmm_host(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, co
     return AFFON_B200_OK;
 }
 
+int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
+                         const void *s, const void *b, void *y, const affon_b200_qmv_fusion *fusion) {
+    t_error.clear();
+    if (!ctx || !fusion || fusion->struct_size != sizeof(affon_b200_qmv_fusion))
+        return fail(AFFON_B200_INVALID_ARG, "qmv_fused: null context or bad fusion descriptor");
+    int rc = validate_desc(desc);
+    if (rc) return rc;
+    if (desc->numerical_policy == AFFON_B200_POLICY_EXACT_ONLY)
+        return fail(AFFON_B200_POLICY_REJECTED,
+                    "numericalPolicy exact_only rejects cuda_quantized_matmul (numerical class reassociated)");
+    afb::QmvFusion f;
+    f.x_mode = fusion->x_mode;
+    f.h_in = fusion->h_in;
+    f.ld_h_in = fusion->ld_h_in;
+    f.ss_in = fusion->ss_in;
+    f.ss_tiles = fusion->ss_tiles;
+    f.gamma = static_cast<const uint16_t *>(fusion->gamma);
+    f.eps = fusion->eps;
+    f.epi = fusion->epilogue;
+    f.h_out = fusion->h_out;
+    f.ld_h_out = fusion->ld_h_out;
+    f.ss_out = fusion->ss_out;
+    f.act = static_cast<uint16_t *>(fusion->act);
+    f.ld_act = fusion->ld_act;
+    f.amax = fusion->amax;
+    if (f.x_mode != 0 && f.x_mode != 1) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: x_mode must be 0 or 1");
+    if (f.epi < 0 || f.epi > 3) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: unknown epilogue");
+    if (f.x_mode == 1 && (!f.h_in || !f.ss_in || !f.gamma || f.ss_tiles <= 0 ||
+                          (reinterpret_cast<uintptr_t>(f.h_in) % 16) || f.ld_h_in % 4))
+        return fail(AFFON_B200_INVALID_ARG, "qmv_fused: rmsnorm prologue needs 16-byte aligned h_in, ss_in, gamma");
+    if ((f.epi == 1 && (!f.h_out || !f.ss_out)) || (f.epi == 2 && !f.act) || (f.epi == 3 && !f.amax) ||
+        (f.epi == 0 && !y))
+        return fail(AFFON_B200_INVALID_ARG, "qmv_fused: missing epilogue buffer");
+    if (f.epi == 2 && desc->w.rows % 16) return fail(AFFON_B200_INVALID_SHAPE, "qmv_fused: silu*mul needs N % 16 == 0");
+    if (!w || !s || !b || (f.x_mode == 0 && !x)) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: null buffer");
+    char *fake = reinterpret_cast<char *>(uintptr_t(1) << 40);
+    afb::QmmArgs a = make_args(desc, x ? x : fake, w, s, b, y ? y : fake);
+    const char *why = "";
+    if (!afb::qmv_supported(a, &why)) return fail(AFFON_B200_UNSUPPORTED, "qmv_fused: %s", why);
+    const afb::QmvPlan plan = afb::qmv_plan(a, ctx->num_sms, ctx->workspace_bytes);
+    if (plan.splits < 1) return fail(AFFON_B200_UNSUPPORTED, "qmv_fused: no plan fits the context workspace");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = afb::launch_qmv(a, plan, ctx->workspace, ctx->stream, &f);
+    if (e != cudaSuccess) return cuda_fail(e, "qmv_fused launch");
+    return AFFON_B200_OK;
+}
+
+int affon_b200_decode_attention(affon_b200_ctx *ctx, const affon_b200_attn_desc *d, const void *qkv, void *k_cache,
+                                void *v_cache, const float *rope_cos, const float *rope_sin, const int *pos,
+                                void *out) {
+    t_error.clear();
+    if (!ctx || !d || d->struct_size != sizeof(affon_b200_attn_desc))
+        return fail(AFFON_B200_INVALID_ARG, "decode_attention: null context or bad descriptor");
+    if (!qkv || !k_cache || !v_cache || !rope_cos || !rope_sin || !pos || !out)
+        return fail(AFFON_B200_INVALID_ARG, "decode_attention: null buffer");
+    if (d->head_dim != 128 || d->kv_heads <= 0 || d->q_heads % d->kv_heads ||
+        (d->q_heads / d->kv_heads != 4 && d->q_heads / d->kv_heads != 8) || d->batch <= 0 || d->capacity <= 0)
+        return fail(AFFON_B200_UNSUPPORTED, "decode_attention: head_dim 128 and 4 or 8 query heads per KV head");
+    if ((reinterpret_cast<uintptr_t>(k_cache) % 16) || (reinterpret_cast<uintptr_t>(v_cache) % 16))
+        return fail(AFFON_B200_INVALID_ARG, "decode_attention: caches must be 16-byte aligned");
+    const size_t need = afb::kPartialOffset + size_t(d->batch) * d->kv_heads * ((d->capacity + 127) / 128) *
+                                                  (d->q_heads / d->kv_heads) * (128 + 2) * 4;
+    if (need > ctx->workspace_bytes || size_t(d->batch) * d->kv_heads > size_t(afb::kMaxTiles))
+        return fail(AFFON_B200_UNSUPPORTED, "decode_attention: partials exceed the context workspace");
+    afb::DecodeAttnArgs a{};
+    a.qkv = qkv;
+    a.ld_qkv = d->ld_qkv;
+    a.q_off = d->q_offset;
+    a.k_off = d->k_offset;
+    a.v_off = d->v_offset;
+    a.k_cache = k_cache;
+    a.v_cache = v_cache;
+    a.rope_cos = rope_cos;
+    a.rope_sin = rope_sin;
+    a.pos = pos;
+    a.out = out;
+    a.ld_out = d->ld_out;
+    a.batch = d->batch;
+    a.q_heads = d->q_heads;
+    a.kv_heads = d->kv_heads;
+    a.head_dim = d->head_dim;
+    a.capacity = d->capacity;
+    a.scale = d->scale;
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = afb::launch_decode_attention(a, ctx->workspace, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "decode_attention launch");
+    return AFFON_B200_OK;
+}
+
+int affon_b200_embed(affon_b200_ctx *ctx, const void *table, int64_t ld_table, const int *tokens, int batch, int dim,
+                     float *h, float *ss_out, unsigned long long *amax) {
+    t_error.clear();
+    if (!ctx || !table || !tokens || !h || !ss_out || !amax || batch <= 0 || batch > 16 || dim <= 0 || dim % 16)
+        return fail(AFFON_B200_INVALID_ARG, "embed: bad arguments (batch <= 16, dim % 16 == 0)");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = afb::launch_embed(table, ld_table, tokens, batch, dim, h, ss_out, amax, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "embed launch");
+    return AFFON_B200_OK;
+}
+
+int affon_b200_argmax_finalize(affon_b200_ctx *ctx, const unsigned long long *amax, int batch, int *tokens,
+                               int *history, int *pos, int *step) {
+    t_error.clear();
+    if (!ctx || !amax || !tokens || !pos || !step || batch <= 0 || batch > 1024)
+        return fail(AFFON_B200_INVALID_ARG, "argmax_finalize: bad arguments");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = afb::launch_finalize(amax, batch, tokens, history, pos, step, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
+    return AFFON_B200_OK;
+}
+
 int affon_b200_compute_core_run_quantized_matmul_f32(const float *activation, size_t activation_count,
                                                      const uint32_t *weights, size_t weight_count, const float *scales,
                                                      size_t scale_count, const float *biases, size_t bias_count,

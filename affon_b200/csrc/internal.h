@@ -42,10 +42,54 @@ struct QmvPlan {
 constexpr size_t kCounterOffset = 256;
 constexpr int64_t kMaxTiles = 262144;
 constexpr size_t kPartialOffset = kCounterOffset + size_t(kMaxTiles) * 4;
+// Optional fusions of the decode qmv (decoder use).  Prologue: the
+// activations are rmsnorm(h) * gamma rounded to bf16, from an f32 residual
+// stream h and per-16-row-tile sums of squares of h written by the previous
+// projection.  Epilogues: store y; add into h and write per-tile sums of
+// squares of the new h; silu(gate) * up into `act` for weights whose 16-row
+// tiles hold 8 gate rows then the matching 8 up rows; per-row argmax packed as
+// (order-preserving key << 32 | ~n) with atomicMax (lowest index wins ties).
+enum QmvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3 };
+struct QmvFusion {
+    int x_mode = 0;                 // 0: bf16 x; 1: rmsnorm of h_in
+    const float *h_in = nullptr;    // [M][ld_h_in] f32
+    int64_t ld_h_in = 0;
+    const float *ss_in = nullptr;   // [ss_tiles][16] f32 sums of squares of h_in rows
+    int ss_tiles = 0;
+    const uint16_t *gamma = nullptr;  // [K] bf16
+    float eps = 1e-5f;
+    int epi = EPI_STORE;
+    float *h_out = nullptr;         // EPI_RESID: [M][ld_h_out] f32, updated in place
+    int64_t ld_h_out = 0;
+    float *ss_out = nullptr;        // EPI_RESID: [N/16][16] f32
+    uint16_t *act = nullptr;        // EPI_SILU_MUL: [M][ld_act] bf16, N/2 columns
+    int64_t ld_act = 0;
+    unsigned long long *amax = nullptr;  // EPI_ARGMAX: [M]
+};
 bool qmv_supported(const QmmArgs &a, const char **why);
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes);
 size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p);
-cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &p, void *workspace, cudaStream_t stream);
+cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &p, void *workspace, cudaStream_t stream,
+                       const QmvFusion *fusion = nullptr);
+
+// Decoder kernels around the quantized linears (decode.cu).
+struct DecodeAttnArgs {
+    const void *qkv;
+    int64_t ld_qkv;
+    int q_off, k_off, v_off;
+    void *k_cache, *v_cache;        // [batch][kv_heads][capacity][head_dim] bf16
+    const float *rope_cos, *rope_sin;  // [capacity][head_dim/2]
+    const int *pos;                 // device scalar: position of the new token
+    void *out;                      // [batch][q_heads*head_dim] bf16
+    int64_t ld_out;
+    int batch, q_heads, kv_heads, head_dim, capacity;
+    float scale;
+};
+cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, cudaStream_t stream);
+cudaError_t launch_embed(const void *table, int64_t ld_table, const int *tokens, int B, int D, float *h, float *ss_out,
+                         unsigned long long *amax, cudaStream_t stream);
+cudaError_t launch_finalize(const unsigned long long *amax, int B, int *tokens, int *history, int *pos, int *step,
+                            cudaStream_t stream);
 
 // Prefill qmm on tcgen05 tensor cores (M >= 64), bf16 x/s/b, 4/8-bit, group 64.
 bool qmm_tc_supported(const QmmArgs &a, const char **why);

@@ -80,6 +80,7 @@ struct Params {
     int stages;           // ring depth
     int max_slots;        // partial slots per block
     int y_bf16;
+    QmvFusion f;
 };
 
 __device__ __forceinline__ uint32_t shr_fma_pipe(uint32_t w, int s) {
@@ -105,6 +106,10 @@ __device__ __forceinline__ void store_out(const Params &p, int m, int64_t n, flo
         static_cast<float *>(p.y)[m * p.ldy + n] = v;
 }
 
+__device__ __forceinline__ const float *base_of_slot(const float *base, int slot, int M, int rows) {
+    return base + static_cast<int64_t>(slot) * M * rows;
+}
+
 // Owner CTA of flat item i when CTA c holds [floor(c*T/C), floor((c+1)*T/C)).
 __device__ __forceinline__ int owner_of(int64_t i, int64_t T, int C) {
     return static_cast<int>(((i + 1) * C - 1) / T);
@@ -123,17 +128,84 @@ __device__ __forceinline__ void contributors(const Params &p, int split, int blk
     }
 }
 
-// Final values of one thread: rows n0+g and n0+g+8, activation rows 2t, 2t+1
-// (+8 for the second MMA column tile).
+__device__ __forceinline__ uint32_t f32_order_key(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Apply the epilogue to the row pair (n_lo, n_lo + 8) of activation row m.
+// Returns the contribution of this pair to the per-tile reductions:
+// EPI_RESID: sum of squares of the updated residual entries; EPI_ARGMAX: the
+// packed best (key << 32 | ~n) of the pair.  Rows at or beyond N are skipped.
+__device__ __forceinline__ unsigned long long epilogue_pair(const Params &p, int m, int64_t n_lo, float v_lo,
+                                                            float v_hi, float &ssq) {
+    const int64_t n_hi = n_lo + 8;
+    const bool ok_lo = n_lo < p.N, ok_hi = n_hi < p.N;
+    unsigned long long best = 0ull;
+    switch (p.f.epi) {
+    case EPI_RESID: {
+        float *h = p.f.h_out + m * p.f.ld_h_out;
+        if (ok_lo) { const float hv = h[n_lo] + v_lo; h[n_lo] = hv; ssq = fmaf(hv, hv, ssq); }
+        if (ok_hi) { const float hv = h[n_hi] + v_hi; h[n_hi] = hv; ssq = fmaf(hv, hv, ssq); }
+        break;
+    }
+    case EPI_SILU_MUL:
+        if (ok_hi) {  // tile rows 0-7 are gate rows, 8-15 the matching up rows
+            const int64_t j = (n_lo >> 4) * 8 + (n_lo & 7);
+            const float gate = v_lo;
+            const float silu = gate / (1.0f + __expf(-gate));
+            p.f.act[m * p.f.ld_act + j] = f32_to_bf16_bits(silu * v_hi);
+        }
+        break;
+    case EPI_ARGMAX:
+        if (ok_lo) best = (static_cast<unsigned long long>(f32_order_key(v_lo)) << 32) | (0xFFFFFFFFu - uint32_t(n_lo));
+        if (ok_hi) {
+            const unsigned long long c =
+                (static_cast<unsigned long long>(f32_order_key(v_hi)) << 32) | (0xFFFFFFFFu - uint32_t(n_hi));
+            best = c > best ? c : best;
+        }
+        break;
+    default:
+        if (ok_lo) store_out(p, m, n_lo, v_lo);
+        if (ok_hi) store_out(p, m, n_hi, v_hi);
+    }
+    return best;
+}
+
+// Reduce a per-pair value over the 8 lanes that share t (lanes t, t+4, ...)
+// and publish it once per (tile, m): sums of squares go to ss_out[tile][m],
+// argmax candidates to amax[m].
+__device__ __forceinline__ void publish_tile(const Params &p, int64_t tile, int m, bool lead, float ssq,
+                                             unsigned long long best) {
+    if (p.f.epi == EPI_RESID) {
+        ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
+        ssq += __shfl_xor_sync(0xffffffffu, ssq, 8);
+        ssq += __shfl_xor_sync(0xffffffffu, ssq, 16);
+        if (lead && m < p.M) p.f.ss_out[tile * 16 + m] = ssq;
+    } else if (p.f.epi == EPI_ARGMAX) {
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lead && m < p.M && best) atomicMax(&p.f.amax[m], best);
+    }
+}
+
+// Final values of one thread for one 16-row tile: rows n0+g and n0+g+8,
+// activation rows 2t, 2t+1 (+8 for the second MMA column tile).  Called by
+// all 32 lanes of the warp.
 template <int MT>
-__device__ __forceinline__ void store_tile(const Params &p, const float (&v)[MT][4], int64_t n0, int g, int t) {
+__device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT][4], int64_t n0, int g, int t) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int m = 2 * t + 8 * mt + (i & 1);
-            const int64_t n = n0 + g + 8 * (i >> 1);
-            if (m < p.M && n < p.N) store_out(p, m, n, v[mt][i]);
+        for (int h = 0; h < 2; ++h) {
+            const int m = 2 * t + 8 * mt + h;
+            float ssq = 0.0f;
+            unsigned long long best = 0ull;
+            if (m < p.M) best = epilogue_pair(p, m, n0 + g, v[mt][h], v[mt][2 + h], ssq);
+            publish_tile(p, n0 >> 4, m, g == 0, ssq, best);
         }
 }
 
@@ -148,11 +220,12 @@ __device__ __forceinline__ void segment_epilogue(const Params &p, float (&acc)[N
     const int64_t nb0 = static_cast<int64_t>(blk) * ROWS;
     if (total == 1) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) store_tile<MT>(p, acc[nt], nb0 + (warp * NT + nt) * 16, g, t);
+        for (int nt = 0; nt < NT; ++nt) finish_tile<MT>(p, acc[nt], nb0 + (warp * NT + nt) * 16, g, t);
         return;
     }
     // partial[((blk * max_slots + slot) * M + m) * ROWS + row]
     float *base = p.partial + (static_cast<int64_t>(blk) * p.max_slots) * p.M * ROWS;
+    float *const base_ptr = base;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -176,14 +249,38 @@ __device__ __forceinline__ void segment_epilogue(const Params &p, float (&acc)[N
     named_bar_sync(1, CW * 32);  // the flag is reused by the next segment
     if (!last) return;
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    // Each warp reduces the rows it owns: lanes over rows, so loads coalesce.
-    for (int r = warp * 16 * NT + lane; r < (warp + 1) * 16 * NT; r += 32) {
-        const int64_t n = nb0 + r;
-        if (n >= p.N) continue;
+    // Each warp reduces the rows it owns, lanes over (row, row+8) pairs of its
+    // tiles so the pair epilogues and per-tile reductions apply unchanged.
+    for (int base = warp * 8 * NT; base < (warp + 1) * 8 * NT; base += 32) {
+        const int pr = base + lane;
+        const bool active = pr < (warp + 1) * 8 * NT;
+        const int r_lo = (pr >> 3) * 16 + (pr & 7);
         for (int m = 0; m < p.M; ++m) {
-            float sum = 0.0f;
-            for (int sl = 0; sl < total; ++sl) sum += __ldcg(&base[(static_cast<int64_t>(sl) * p.M + m) * ROWS + r]);
-            store_out(p, m, n, sum);
+            float ssq = 0.0f;
+            unsigned long long best = 0ull;
+            if (active) {
+                float lo = 0.0f, hi = 0.0f;
+                for (int sl = 0; sl < total; ++sl) {
+                    const float *slot_base = base_of_slot(base_ptr, sl, p.M, ROWS) + static_cast<int64_t>(m) * ROWS;
+                    lo += __ldcg(&slot_base[r_lo]);
+                    hi += __ldcg(&slot_base[r_lo + 8]);
+                }
+                best = epilogue_pair(p, m, nb0 + r_lo, lo, hi, ssq);
+            }
+            // lanes pr..pr+7 share a tile: reduce over the low 3 lane bits
+            if (p.f.epi == EPI_RESID) {
+                ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
+                ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
+                ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
+                if (active && (pr & 7) == 0) p.f.ss_out[((nb0 + r_lo) >> 4) * 16 + m] = ssq;
+            } else if (p.f.epi == EPI_ARGMAX) {
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+                    best = other > best ? other : best;
+                }
+                if (active && (pr & 7) == 0 && best) atomicMax(&p.f.amax[m], best);
+            }
         }
     }
     if (tid == 0) atomicExch(&p.counters[blk], 0u);
@@ -193,9 +290,37 @@ __device__ __forceinline__ void segment_epilogue(const Params &p, float (&acc)[N
 // the consumer warps only.
 template <int BITS>
 __device__ __forceinline__ void stage_x(const Params &p, char *xs, float *xg, int xs_rs, int64_t k0, int tid,
-                                        int nthreads) {
+                                        int nthreads, float *rms, float *red) {
     const int gs = p.ks / GROUP;
     for (int i = tid; i < gs * 16; i += nthreads) xg[i] = 0.0f;
+    if (p.f.x_mode == 1) {
+        // 1/rms of every activation row from the per-tile sums of squares
+        // (fixed summation order: per thread, then per warp, then per CTA).
+        float acc[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) acc[m] = 0.0f;
+        for (int tl = tid; tl < p.f.ss_tiles; tl += nthreads) {
+            const float4 *src = reinterpret_cast<const float4 *>(p.f.ss_in + static_cast<int64_t>(tl) * 16);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = __ldcg(src + q);
+                acc[4 * q] += v.x; acc[4 * q + 1] += v.y; acc[4 * q + 2] += v.z; acc[4 * q + 3] += v.w;
+            }
+        }
+        const int lane = tid & 31, w = tid >> 5;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+#pragma unroll
+            for (int o = 16; o; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+            if (lane == 0) red[w * 16 + m] = acc[m];
+        }
+        named_bar_sync(1, nthreads);
+        if (tid < 16) {
+            float sum = 0.0f;
+            for (int ww = 0; ww < nthreads / 32; ++ww) sum += red[ww * 16 + tid];
+            rms[tid] = rsqrtf(sum / static_cast<float>(p.K) + p.f.eps);
+        }
+    }
     named_bar_sync(1, nthreads);
     const int cpr = p.ks / 8;  // 16-byte chunks per row
     const int total = p.M * cpr;
@@ -204,7 +329,23 @@ __device__ __forceinline__ void stage_x(const Params &p, char *xs, float *xg, in
         const bool valid = c < total;
         const int m = valid ? c / cpr : 0, kc = valid ? c % cpr : 0;
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid) v = ldg_nc_v4(p.x + m * p.ldx + k0 + kc * 8);
+        if (valid) {
+            if (p.f.x_mode == 1) {  // x = bf16(h * rms * gamma)
+                const float4 *hp = reinterpret_cast<const float4 *>(p.f.h_in + m * p.f.ld_h_in + k0 + kc * 8);
+                const float4 h0 = __ldcg(hp), h1 = __ldcg(hp + 1);
+                const uint4 gm = ldg_nc_v4(p.f.gamma + k0 + kc * 8);
+                const float r = rms[m];
+                auto nb = [&](float hv, uint32_t gw, int hi) {
+                    return f32_to_bf16_bits(hv * r * bf16_bits_to_f32(hi ? (gw >> 16) : (gw & 0xFFFF)));
+                };
+                v.x = nb(h0.x, gm.x, 0) | (uint32_t(nb(h0.y, gm.x, 1)) << 16);
+                v.y = nb(h0.z, gm.y, 0) | (uint32_t(nb(h0.w, gm.y, 1)) << 16);
+                v.z = nb(h1.x, gm.z, 0) | (uint32_t(nb(h1.y, gm.z, 1)) << 16);
+                v.w = nb(h1.z, gm.w, 0) | (uint32_t(nb(h1.w, gm.w, 1)) << 16);
+            } else {
+                v = ldg_nc_v4(p.x + m * p.ldx + k0 + kc * 8);
+            }
+        }
         float sum = bf16_bits_to_f32(v.x & 0xFFFF) + bf16_bits_to_f32(v.x >> 16) + bf16_bits_to_f32(v.y & 0xFFFF) +
                     bf16_bits_to_f32(v.y >> 16) + bf16_bits_to_f32(v.z & 0xFFFF) + bf16_bits_to_f32(v.z >> 16) +
                     bf16_bits_to_f32(v.w & 0xFFFF) + bf16_bits_to_f32(v.w >> 16);
@@ -245,6 +386,8 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
     uint64_t *empty = full + MAX_STAGES;
     volatile int *abort = reinterpret_cast<volatile int *>(empty + MAX_STAGES);
     volatile int *flag = abort + 1;
+    float *rms = reinterpret_cast<float *>(empty + MAX_STAGES) + 4;  // [16]
+    float *red = rms + 16;                                            // [CW][16]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
@@ -302,7 +445,7 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
         const int64_t seg_end = min(hi, blk_begin + p.spb);
         if (split != cur_split) {
             named_bar_sync(1, CW * 32);
-            stage_x<BITS>(p, xs, xg, xs_rs, static_cast<int64_t>(split) * p.ks, tid, CW * 32);
+            stage_x<BITS>(p, xs, xg, xs_rs, static_cast<int64_t>(split) * p.ks, tid, CW * 32, rms, red);
             cur_split = split;
         }
         float acc[NT][MT][4];
@@ -480,7 +623,7 @@ QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     QmvPlan p{};
     const Variant v = variant_of(a);
     const int nk = static_cast<int>(a.K / 512);
-    const int overhead = 1024 + 2 * qmv::MAX_STAGES * 8 + 64;
+    const int overhead = 1024 + 2 * qmv::MAX_STAGES * 8 + 64 + 20 * 16 * 4;
     // K splits: the smallest count whose x slice fits next to the ring, raised
     // towards the count that balances the two on-chip costs of stream-K --
     // every CTA stages its x slice (grid * M * K/S * 2 bytes) while every
@@ -540,7 +683,8 @@ static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, cons
     return cudaGetLastError();
 }
 
-cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, cudaStream_t stream) {
+cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, cudaStream_t stream,
+                       const QmvFusion *fusion) {
     if (plan.splits < 1) return cudaErrorInvalidValue;
     const Variant v = variant_of(a);
     qmv::Params p{};
@@ -559,6 +703,7 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     p.stages = plan.stages;
     p.max_slots = plan.max_slots;
     p.y_bf16 = a.y_bf16;
+    if (fusion) p.f = *fusion;
     char *ws = static_cast<char *>(workspace);
     p.status = reinterpret_cast<unsigned *>(ws);
     p.counters = reinterpret_cast<unsigned *>(ws + kCounterOffset);

@@ -2,10 +2,13 @@
 """Benchmark of the quantized-linear hot path on B200.
 
 Workloads (--workload):
-  qmv   BASELINE config 2 headline: one decode qmv of the largest sweep shape,
-        M=16, 4-bit, group 64, N=128256, K=4096 (the LM-head projection).  A
-        step is one qmv over that weight; the weight (282 MB) exceeds L2, so
-        every step streams it from HBM.
+  decode  (default) BASELINE config 4: Llama-3-8B-shaped decoder, all linears
+          4-bit affine group 64, batch 16, KV cache prefilled from a random
+          1024-token sequence; a step is one decode step (16 tokens), captured
+          in a CUDA graph.  Metric: decode tok/s.
+  qmv     BASELINE config 2 headline shape: one decode qmv, M=16, 4-bit,
+          group 64, N=128256, K=4096 (the LM-head projection); the weight
+          (282 MB) exceeds L2, so every step streams it from HBM.
 
 Output: one JSON line on rank 0 (the driver's contract): value = whole-job
 throughput with inputs resident in HBM; e2e = the same metric through the
@@ -241,6 +244,192 @@ def run_qmv(args, rank, world, dev):
     }
 
 
+def _graph_time_ms(fn, reps, dev):
+    """Average device time of fn() captured `reps` times in one CUDA graph."""
+    import torch
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        fn(s)
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn(s)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / reps
+
+
+def run_decode(args, rank, world, dev):
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from affon_b200 import _lib
+    from affon_b200.core import check
+    from affon_b200.decoder import LLAMA3_8B, QuantizedDecoder, weight_bytes
+
+    cfg = LLAMA3_8B
+    B, ctxlen = 16, 1024
+    cap = ctxlen + args.warmup + 2 * args.steps + 8
+    dec = QuantizedDecoder(cfg, B, cap, dev, seed=0, max_steps=args.warmup + 2 * args.steps + 8)
+    gen = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (ctxlen, B), generator=gen)
+    dec.capture()
+    t0 = time.time()
+    dec.prefill(prompt)                     # positions 0..1023 through the same graph
+    torch.cuda.synchronize(dev)
+    prefill_s = time.time() - t0
+    dec.reset(ctxlen)
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        dec.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    pos0 = int(dec.pos.item())
+    launches0 = L.affon_b200_launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            dec.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    # graph replays do not pass through the C ABI, so count the launches of one
+    # captured step (embed + per layer 4 qmv + attention, LM head, finalize)
+    launches = args.steps * (2 + 5 * cfg.layers + 1)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    tok_s = B * world / (ms_max * 1e-3)
+    # bytes per step at the mean position of the timed steps
+    mid = pos0 + args.steps // 2
+    step_bytes = dec.step_bytes(mid)
+    wbytes = weight_bytes(cfg)
+
+    # e2e: each step copies its input tokens from pinned host memory and reads
+    # the sampled tokens back, inside the timed region.
+    tok_h = torch.empty((B,), dtype=torch.int32).pin_memory()
+    out_h = torch.empty((B,), dtype=torch.int32).pin_memory()
+    tok_h.copy_(dec.tokens.cpu())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(args.steps):
+        dec.tokens.copy_(tok_h, non_blocking=True)
+        dec.replay()
+        out_h.copy_(dec.tokens, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()  # the host reads the step's tokens
+        tok_h.copy_(out_h)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # dominant kernel, timed live: the gate/up qmv of layer 0 (largest share of
+    # the weight bytes), with its fused rmsnorm prologue and silu*mul epilogue
+    lay = dec.layers[0]
+    gu = lay["gate_up"]
+    desc = gu.desc(B)
+    fus = None
+    for call in dec.calls:
+        if call[0] == "qmv" and call[3] is gu:
+            fus = call[5]
+    def gu_launch(s):
+        check(L.affon_b200_ctx_set_stream(dec.ctx, s.cuda_stream))
+        check(L.affon_b200_qmv_fused(dec.ctx, ctypes.byref(desc), None, gu.w.data_ptr(), gu.s.data_ptr(),
+                                     gu.b.data_ptr(), None, ctypes.byref(fus)))
+    # rotate over all 32 layers' gate/up weights so launches stream from HBM
+    gus = [l["gate_up"] for l in dec.layers]
+    idx = [0]
+    def gu_launch_rot(s):
+        lin = gus[idx[0] % len(gus)]
+        idx[0] += 1
+        check(L.affon_b200_ctx_set_stream(dec.ctx, s.cuda_stream))
+        check(L.affon_b200_qmv_fused(dec.ctx, ctypes.byref(desc), None, lin.w.data_ptr(), lin.s.data_ptr(),
+                                     lin.b.data_ptr(), None, ctypes.byref(fus)))
+    gu_ms = _graph_time_ms(gu_launch_rot, 64, dev)
+    dec.set_stream(torch.cuda.current_stream(dev))
+    gu_bytes = gu.N * gu.K * gu.bits // 8 + gu.N * (gu.K // 64) * 4 + B * gu.K * 4 + B * (gu.N // 2) * 2
+    dec.close()
+
+    pk, pk_kind = peaks()
+    roof_tok_s = B / (step_bytes / (pk["hbm_gbs"] * 1e9))
+    roof_w_tok_s = B / (wbytes / (pk["hbm_gbs"] * 1e9))
+    gu_achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "ncu_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("qmv_gate_up_m16_b4_n28672_k4096")
+    return {
+        "metric": "4-bit decode tok/s (Llama-3-8B shape, batch 16, 1024 context)", "value": round(tok_s, 1),
+        "unit": "tok/s", "ms_per_step": round(ms_max, 4), "higher_is_better": True,
+        "dtype": "u4 codes x bf16 -> f32 accumulate, bf16 activations",
+        "config": {"workload": "decode_llama3_8b_b16_ctx1024", "model": "llama3-8b-shape (random init, 4-bit g64)",
+                   "global_batch": B, "seq_len": ctxlen, "layers": cfg.layers, "d_model": cfg.d_model,
+                   "ffn": cfg.ffn, "vocab": cfg.vocab, "kv_cache": "prefilled by 1024 teacher-forced decode steps",
+                   "prefill_seconds": round(prefill_s, 2), "l2": "weights 4.2 GB >> L2",
+                   "step_hbm_bytes": step_bytes, "weight_bytes": wbytes,
+                   "roofline_tok_s_weights_plus_kv": round(roof_tok_s, 1),
+                   "frac_of_weights_plus_kv_roofline": round(tok_s / world / roof_tok_s, 4),
+                   "roofline_tok_s_weights_only": round(roof_w_tok_s, 1),
+                   "frac_of_weights_only_roofline": round(tok_s / world / roof_w_tok_s, 4),
+                   "step_achieved_gbs": round(step_bytes / (ms_max * 1e-3) / 1e9, 1)},
+        "e2e": {"value": round(B * world / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 4,
+                "d2h_bytes_per_step": B * 4, "ms_per_step": round(e2e_ms, 4),
+                "path": "decoder graph replay with pinned token H2D/D2H and host read each step"},
+        "roofline": {"bound": "hbm", "kernel": "qmv gate/up (rmsnorm prologue, silu*mul epilogue), M=16 N=28672 K=4096",
+                     "achieved": round(gu_achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gu_achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+                     "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json)" if pk_kind == "measured" else
+                     "fallback 6.65 TB/s", "algorithmic_bytes_per_launch": gu_bytes,
+                     "launch_us": round(gu_ms * 1e3, 2)},
+        "gpu_launches": int(launches), "clocks": clocks.summary(), "_rank0_ms": ms,
+    }
+
+
+def cpu_baseline_decode(args, threads, seconds_target=15.0):
+    """CPU oracle on a bounded sample of the decode step: M=16 rows through
+    a slice of a K=4096 projection, scaled to the whole step's weights.
+    Only the quantized linears are counted (attention and norms are left
+    out), which favours the CPU."""
+    import oracle
+    from affon_b200 import synthetic
+    from affon_b200.decoder import LLAMA3_8B, linear_param_count
+    M, K = 16, 4096
+    rows = 256 * max(1, threads)
+    data = synthetic.quantized_linear(M, rows, K, bits=4, group=64, seed=0)
+    times = []
+    t_end = time.time() + seconds_target
+    while time.time() < t_end or not times:
+        t0 = time.perf_counter()
+        oracle.qmm_dense(data["x"], "bf16", data["w"], data["s"], data["b"], "bf16", M, rows, K, 4, 64,
+                         threads=threads)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 50:
+            break
+    t = statistics.median(times)
+    step_s = t * linear_param_count(LLAMA3_8B) / (rows * K)
+    return {"value": round(M / step_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"M=16 x {rows} weight rows x K=4096 (4-bit) per run, median of {len(times)} runs "
+                      f"({t * 1e3:.1f} ms), scaled by the 7.5e9 linear weights of a step; attention and norms "
+                      f"not counted"}
+
+
 def cpu_baseline_qmv(args, threads, seconds_target=15.0):
     """Oracle on a bounded row sample of the qmv workload; GB/s of algorithmic bytes."""
     import oracle
@@ -278,7 +467,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="affon_b200", choices=["affon_b200", "reference"])
-    ap.add_argument("--workload", default="qmv", choices=["qmv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "qmv"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -290,22 +479,23 @@ def main():
         if rank != 0:
             return 0
         th = host_threads()
-        steps = []
-        for _ in range(args.warmup):
-            pass
-        base = None
+        base_fn = cpu_baseline_decode if args.workload == "decode" else cpu_baseline_qmv
+        metric = ("4-bit decode tok/s (Llama-3-8B shape, batch 16, 1024 context)" if args.workload == "decode"
+                  else "qmv GB/s (4-bit decode, M=16, N=128256, K=4096)")
+        unit = "tok/s" if args.workload == "decode" else "GB/s"
+        workload = "decode_llama3_8b_b16_ctx1024" if args.workload == "decode" else "qmv_m16_b4_g64_n128256_k4096"
+        vals, base = [], None
         for _ in range(args.steps):
-            base = cpu_baseline_qmv(args, th, seconds_target=2.0)
-            steps.append(base["value"])
-        value = statistics.median(steps)
-        line = {"metric": "qmv GB/s (4-bit decode, M=16, N=128256, K=4096)", "value": value, "unit": "GB/s",
-                "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 widened)",
-                "data": "synthetic", "config": {"workload": "qmv_m16_b4_g64_n128256_k4096"},
-                "cpu_baseline": {**base, "value": value},
-                "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            base = base_fn(args, th, seconds_target=2.0)
+            vals.append(base["value"])
+        value = statistics.median(vals)
+        line = {"metric": metric, "value": value, "unit": unit, "impl": "reference", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32 (bf16 widened)", "data": "synthetic",
+                "config": {"workload": workload}, "cpu_baseline": {**base, "value": value},
+                "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                 "note": "reference CPU kernel (compute/src/backend/cpu/quantized_matmul.zig) is not vendored and "
-                        "needs zig; its C restatement (oracle/) runs instead, all host threads"}
+                        "needs zig; its C restatement (oracle/) runs instead, on all host threads"}
         print(json.dumps(line))
         return 0
 
@@ -317,13 +507,14 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    res = run_qmv(args, rank, world, dev)
+    res = run_decode(args, rank, world, dev) if args.workload == "decode" else run_qmv(args, rank, world, dev)
     if rank == 0:
         res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "weak",
-                    "vs_baseline": None, "data": "synthetic (seeded, BASELINE distributions)"})
+                    "vs_baseline": None, "data": "synthetic (seeded random weights and tokens, BASELINE "
+                                                  "distributions)"})
         res["config"]["parallelism"] = f"replicas{world}" if world > 1 else "single"
         if not args.no_cpu_baseline:
-            res["cpu_baseline"] = cpu_baseline_qmv(args, 1)
+            res["cpu_baseline"] = (cpu_baseline_decode if args.workload == "decode" else cpu_baseline_qmv)(args, 1)
         res.pop("_rank0_ms", None)
         order = ["metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
                  "scaling", "vs_baseline", "dtype", "data", "config", "e2e", "roofline", "cpu_baseline",

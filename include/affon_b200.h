@@ -182,6 +182,72 @@ int affon_b200_compute_core_run_quantized_matmul_f32(
 int affon_b200_qmv_noalloc(const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w, const void *s,
                            const void *b, void *y, void *cuda_stream);
 
+/* ---------------------------------------------------------------------------
+ * Decoder building blocks.  No counterpart in the reference, which has no
+ * quantized decoder (packages/@affon/models/src/llama/model.ts:64-78 uses
+ * dense matmuls); they run the BASELINE Llama-shaped decode around the
+ * quantized linears, with the decoder's norms, residual adds, gated
+ * activation and argmax fused into the qmv. */
+
+/* Fusions of the decode qmv.  x_mode 1: the activations are
+ * bf16(h_in[m][k] * rsqrt(sum_k h_in[m][k]^2 / K + eps) * gamma[k]), the sum
+ * taken from ss_in ([ss_tiles][16] f32 partial sums, any order of tiles,
+ * summed in a fixed order).  epilogue 1: h_out[m][n] += y[m][n] (f32) and
+ * ss_out[n/16][m] = sum of the squares of the 16 updated h_out entries;
+ * epilogue 2: act[m][8*(n/16) + n%8] = bf16(silu(y[m][n]) * y[m][n+8]) for
+ * n%16 < 8 (weight tiles of 8 gate rows then the 8 matching up rows);
+ * epilogue 3: atomicMax(amax[m], key(y[m][n]) << 32 | (0xffffffff - n)) with an
+ * order-preserving key (lowest index wins ties; amax must start at 0). */
+typedef struct affon_b200_qmv_fusion {
+    uint32_t struct_size;
+    int32_t x_mode;
+    const float *h_in;
+    int64_t ld_h_in;
+    const float *ss_in;
+    int32_t ss_tiles;
+    float eps;
+    const void *gamma;
+    int32_t epilogue;
+    int32_t reserved;
+    float *h_out;
+    int64_t ld_h_out;
+    float *ss_out;
+    void *act;
+    int64_t ld_act;
+    unsigned long long *amax;
+} affon_b200_qmv_fusion;
+
+int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
+                         const void *s, const void *b, void *y, const affon_b200_qmv_fusion *fusion);
+
+/* Grouped-query decode attention over a [batch][kv_heads][capacity][128] bf16
+ * KV cache: RoPE (rotate-half pairs, tables [capacity][64]) on the queries
+ * and the new key, the new key/value written at *pos, softmax over positions
+ * 0..*pos, output [batch][q_heads*128] bf16.  q/k/v are columns q_offset,
+ * k_offset, v_offset of the bf16 rows of qkv. */
+typedef struct affon_b200_attn_desc {
+    uint32_t struct_size;
+    int32_t batch, q_heads, kv_heads, head_dim, capacity;
+    float scale;
+    int32_t q_offset, k_offset, v_offset;
+    int32_t reserved;
+    int64_t ld_qkv, ld_out;
+} affon_b200_attn_desc;
+
+int affon_b200_decode_attention(affon_b200_ctx *ctx, const affon_b200_attn_desc *desc, const void *qkv,
+                                void *k_cache, void *v_cache, const float *rope_cos, const float *rope_sin,
+                                const int *pos, void *out);
+
+/* h[b][:] = f32(table[tokens[b]][:]) with ss_out[dim/16][16] partial sums of
+ * squares for the first norm; also zeroes amax[0..batch). */
+int affon_b200_embed(affon_b200_ctx *ctx, const void *table, int64_t ld_table, const int *tokens, int batch, int dim,
+                     float *h, float *ss_out, unsigned long long *amax);
+
+/* tokens[b] = argmax index held in amax[b]; history[*step][b] = tokens[b]
+ * (history may be NULL); then *pos += 1 and *step += 1. */
+int affon_b200_argmax_finalize(affon_b200_ctx *ctx, const unsigned long long *amax, int batch, int *tokens,
+                               int *history, int *pos, int *step);
+
 /* Number of kernel launches this library issued in this process (all
  * contexts); lets callers and benchmarks count native launches. */
 uint64_t affon_b200_launch_count(void);
