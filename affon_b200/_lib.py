@@ -29,16 +29,16 @@ class QmmDesc(ctypes.Structure):
 
 
 class QmvFusion(ctypes.Structure):
-    _fields_ = [("struct_size", c_u32), ("x_mode", c_i32), ("h_in", c_vp), ("ld_h_in", c_i64), ("ss_in", c_vp),
-                ("ss_tiles", c_i32), ("eps", ctypes.c_float), ("gamma", c_vp), ("epilogue", c_i32),
-                ("reserved", c_i32), ("h_out", c_vp), ("ld_h_out", c_i64), ("ss_out", c_vp), ("act", c_vp),
-                ("ld_act", c_i64), ("amax", c_vp)]
+    _fields_ = [("struct_size", c_u32), ("x_mode", c_i32), ("epilogue", c_i32), ("act_pair_order", c_i32),
+                ("h_out", c_vp), ("ld_h_out", c_i64), ("ss_out", c_vp), ("act", c_vp), ("ld_act", c_i64),
+                ("amax", c_vp)]
 
 
 class AttnDesc(ctypes.Structure):
     _fields_ = [("struct_size", c_u32), ("batch", c_i32), ("q_heads", c_i32), ("kv_heads", c_i32),
                 ("head_dim", c_i32), ("capacity", c_i32), ("scale", ctypes.c_float), ("q_offset", c_i32),
-                ("k_offset", c_i32), ("v_offset", c_i32), ("reserved", c_i32), ("ld_qkv", c_i64), ("ld_out", c_i64)]
+                ("k_offset", c_i32), ("v_offset", c_i32), ("out_pair_order", c_i32), ("ld_qkv", c_i64),
+                ("ld_out", c_i64)]
 
 
 EPI_STORE, EPI_RESID, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
@@ -70,6 +70,8 @@ SIGNATURES = {
     "affon_b200_qmv_noalloc": ([ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
     "affon_b200_qmv_fused": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp,
                               ctypes.POINTER(QmvFusion)], c_i32),
+    "affon_b200_qmv_prep": ([c_vp, c_i32, c_vp, c_i64, c_vp, c_i32, c_vp, ctypes.c_float, c_i32, c_i32, c_i32, c_vp,
+                             c_i64], c_i32),
     "affon_b200_decode_attention": ([c_vp, ctypes.POINTER(AttnDesc), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
     "affon_b200_embed": ([c_vp, c_vp, c_i64, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp], c_i32),
     "affon_b200_argmax_finalize": ([c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp], c_i32),

@@ -181,8 +181,9 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
     if (qmv_plannable && a.M <= 16) {
         c.impl = IMPL_QMV;
         c.plan = qplan;
-        snprintf(reason, sizeof reason, "M=%lld <= 16: decode qmv, stream-K over %d CTAs, %d K splits, %d-stage ring",
-                 (long long)a.M, c.plan.grid_n, c.plan.splits, c.plan.stages);
+        snprintf(reason, sizeof reason,
+                 "M=%lld <= 16: decode qmv, stream-K over %d CTAs, up to %d K segments per tile, %d-stage ring",
+                 (long long)a.M, c.plan.grid_n, c.plan.max_slots, c.plan.stages);
     } else if (tc_ok && (d->numerical_policy == AFFON_B200_POLICY_APPROXIMATE || a.y_bf16)) {
         c.impl = IMPL_QMM_TC;
         snprintf(reason, sizeof reason, "M=%lld >= 64: tcgen05 qmm with bf16-rounded decoded weights", (long long)a.M);
@@ -207,7 +208,7 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
             snprintf(sel->implementation_id, sizeof sel->implementation_id, "cuda_quantized_matmul.sm100_generic");
         sel->implementation_version = 1;
         sel->numerical_class = c.impl == IMPL_QMM_TC ? AFFON_B200_APPROXIMATE : AFFON_B200_REASSOCIATED;
-        sel->splits = c.impl == IMPL_QMV ? c.plan.splits : 1;
+        sel->splits = c.impl == IMPL_QMV ? c.plan.max_slots : 1;  // K segments combined per output tile
         snprintf(sel->reason, sizeof sel->reason, "%s", reason);
     }
     *out = c;
@@ -451,31 +452,23 @@ int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, c
                     "numericalPolicy exact_only rejects cuda_quantized_matmul (numerical class reassociated)");
     afb::QmvFusion f;
     f.x_mode = fusion->x_mode;
-    f.h_in = fusion->h_in;
-    f.ld_h_in = fusion->ld_h_in;
-    f.ss_in = fusion->ss_in;
-    f.ss_tiles = fusion->ss_tiles;
-    f.gamma = static_cast<const uint16_t *>(fusion->gamma);
-    f.eps = fusion->eps;
     f.epi = fusion->epilogue;
     f.h_out = fusion->h_out;
     f.ld_h_out = fusion->ld_h_out;
     f.ss_out = fusion->ss_out;
     f.act = static_cast<uint16_t *>(fusion->act);
     f.ld_act = fusion->ld_act;
+    f.act_pair_order = fusion->act_pair_order;
     f.amax = fusion->amax;
     if (f.x_mode != 0 && f.x_mode != 1) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: x_mode must be 0 or 1");
     if (f.epi < 0 || f.epi > 3) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: unknown epilogue");
-    if (f.x_mode == 1 && (!f.h_in || !f.ss_in || !f.gamma || f.ss_tiles <= 0 ||
-                          (reinterpret_cast<uintptr_t>(f.h_in) % 16) || f.ld_h_in % 4))
-        return fail(AFFON_B200_INVALID_ARG, "qmv_fused: rmsnorm prologue needs 16-byte aligned h_in, ss_in, gamma");
     if ((f.epi == 1 && (!f.h_out || !f.ss_out)) || (f.epi == 2 && !f.act) || (f.epi == 3 && !f.amax) ||
         (f.epi == 0 && !y))
         return fail(AFFON_B200_INVALID_ARG, "qmv_fused: missing epilogue buffer");
     if (f.epi == 2 && desc->w.rows % 16) return fail(AFFON_B200_INVALID_SHAPE, "qmv_fused: silu*mul needs N % 16 == 0");
-    if (!w || !s || !b || (f.x_mode == 0 && !x)) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: null buffer");
+    if (!w || !s || !b || !x) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: null buffer");
     char *fake = reinterpret_cast<char *>(uintptr_t(1) << 40);
-    afb::QmmArgs a = make_args(desc, x ? x : fake, w, s, b, y ? y : fake);
+    afb::QmmArgs a = make_args(desc, x, w, s, b, y ? y : fake);
     const char *why = "";
     if (!afb::qmv_supported(a, &why)) return fail(AFFON_B200_UNSUPPORTED, "qmv_fused: %s", why);
     const afb::QmvPlan plan = afb::qmv_plan(a, ctx->num_sms, ctx->workspace_bytes);
@@ -483,6 +476,24 @@ int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, c
     DeviceGuard guard(ctx->device);
     cudaError_t e = afb::launch_qmv(a, plan, ctx->workspace, ctx->stream, &f);
     if (e != cudaSuccess) return cuda_fail(e, "qmv_fused launch");
+    return AFFON_B200_OK;
+}
+
+int affon_b200_qmv_prep(affon_b200_ctx *ctx, int mode, const void *src, int64_t ld_src, const float *ss,
+                        int ss_tiles, const void *gamma, float eps, int rows, int cols, int bits, void *dst,
+                        int64_t ld_dst) {
+    t_error.clear();
+    if (!ctx || !src || !dst || rows <= 0 || rows > 16 || cols <= 0 || cols % 8 || (bits != 4 && bits != 8) ||
+        (mode != 0 && mode != 1) || ld_src % 8 || ld_dst % 8)
+        return fail(AFFON_B200_INVALID_ARG, "qmv_prep: bad arguments");
+    if (mode == 1 && (!ss || !gamma || ss_tiles <= 0))
+        return fail(AFFON_B200_INVALID_ARG, "qmv_prep: rmsnorm needs ss and gamma");
+    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; };
+    if (!al16(src) || !al16(dst) || (gamma && !al16(gamma))) return fail(AFFON_B200_INVALID_ARG, "qmv_prep: alignment");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = afb::launch_qmv_prep(src, ld_src, mode, ss, ss_tiles, static_cast<const uint16_t *>(gamma), eps,
+                                         rows, cols, bits, static_cast<uint16_t *>(dst), ld_dst, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "qmv_prep launch");
     return AFFON_B200_OK;
 }
 
@@ -522,6 +533,7 @@ int affon_b200_decode_attention(affon_b200_ctx *ctx, const affon_b200_attn_desc 
     a.head_dim = d->head_dim;
     a.capacity = d->capacity;
     a.scale = d->scale;
+    a.out_pair_order = d->out_pair_order;
     DeviceGuard guard(ctx->device);
     cudaError_t e = afb::launch_decode_attention(a, ctx->workspace, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "decode_attention launch");

@@ -42,6 +42,7 @@ struct AttnParams {
     unsigned *status;
     int B, QH, KVH, cap, max_chunks;
     float scale;
+    int out_pair_order;
 };
 
 template <int G>
@@ -144,23 +145,23 @@ __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_
 #pragma unroll
     for (int h = 0; h < G; ++h) ps[h * CH + tid] = sc[h];
     __syncthreads();
-    // Softmax statistics: warp h handles head h (G <= 4 warps).
-    if (warp < G) {
+    // Softmax statistics: warp w handles heads w, w+4, ...
+    for (int hh = warp; hh < G; hh += THREADS / 32) {
         float v[CH / 32], mx = -INFINITY;
 #pragma unroll
-        for (int k = 0; k < CH / 32; ++k) { v[k] = ps[warp * CH + lane + 32 * k]; mx = fmaxf(mx, v[k]); }
+        for (int k = 0; k < CH / 32; ++k) { v[k] = ps[hh * CH + lane + 32 * k]; mx = fmaxf(mx, v[k]); }
 #pragma unroll
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float sum = 0.0f;
 #pragma unroll
         for (int k = 0; k < CH / 32; ++k) {
             const float e = (v[k] == -INFINITY) ? 0.0f : __expf(v[k] - mx);
-            ps[warp * CH + lane + 32 * k] = e;
+            ps[hh * CH + lane + 32 * k] = e;
             sum += e;
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) { stat[warp] = mx; stat[G + warp] = sum; }
+        if (lane == 0) { stat[hh] = mx; stat[G + hh] = sum; }
     }
     __syncthreads();
     // Unnormalised outputs: thread d accumulates o[h][d] over the chunk.
@@ -192,7 +193,10 @@ __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_
     __syncthreads();
     if (!*flag) return;
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    // Merge the chunks in order.
+    // Merge the chunks in order.  Output column of this thread: d, or its
+    // slot in the 4-bit qmv pair order (within 8 columns: 0 4 1 5 2 6 3 7).
+    const int e8 = tid & 7;
+    const int out_col = p.out_pair_order ? (tid & ~7) + (e8 < 4 ? 2 * e8 : 2 * (e8 - 4) + 1) : tid;
     const float *recs = p.partial + static_cast<int64_t>(pair) * p.max_chunks * (G * (HD + 2));
 #pragma unroll
     for (int h = 0; h < G; ++h) {
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_
             L = fmaf(__ldcg(&r[G + h]), w, L);
             O = fmaf(__ldcg(&r[2 * G + h * HD + tid]), w, O);
         }
-        p.out[b * p.ld_out + (kvh * G + h) * HD + tid] = f32_to_bf16_bits(O / L);
+        p.out[b * p.ld_out + (kvh * G + h) * HD + out_col] = f32_to_bf16_bits(O / L);
     }
     if (tid == 0) atomicExch(&p.counters[pair], 0u);
 }
@@ -271,6 +275,7 @@ cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, cu
     p.cap = a.capacity;
     p.max_chunks = (a.capacity + dec::CH - 1) / dec::CH;
     p.scale = a.scale;
+    p.out_pair_order = a.out_pair_order;
     char *ws = static_cast<char *>(workspace);
     p.status = reinterpret_cast<unsigned *>(ws);
     p.counters = reinterpret_cast<unsigned *>(ws + kCounterOffset);

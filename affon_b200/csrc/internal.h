@@ -42,33 +42,39 @@ struct QmvPlan {
 constexpr size_t kCounterOffset = 256;
 constexpr int64_t kMaxTiles = 262144;
 constexpr size_t kPartialOffset = kCounterOffset + size_t(kMaxTiles) * 4;
-// Optional fusions of the decode qmv (decoder use).  Prologue: the
-// activations are rmsnorm(h) * gamma rounded to bf16, from an f32 residual
-// stream h and per-16-row-tile sums of squares of h written by the previous
-// projection.  Epilogues: store y; add into h and write per-tile sums of
-// squares of the new h; silu(gate) * up into `act` for weights whose 16-row
-// tiles hold 8 gate rows then the matching 8 up rows; per-row argmax packed as
-// (order-preserving key << 32 | ~n) with atomicMax (lowest index wins ties).
+// Optional fusions of the decode qmv (decoder use).  Activations: natural
+// bf16 x (x_mode 0; 4-bit codes then convert it into the workspace tail) or
+// x already in the kernel's column order (x_mode 1, written by
+// launch_qmv_prep or by a fused producer).  Epilogues: store y; add into h
+// and write per-16-row-tile sums of squares of the new h; silu(gate) * up
+// into `act` for weights whose 16-row tiles hold 8 gate rows then the
+// matching 8 up rows (optionally in the 4-bit pair order); per-row argmax
+// packed as (order-preserving key << 32 | ~n) with atomicMax (lowest index
+// wins ties).
 enum QmvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3 };
 struct QmvFusion {
-    int x_mode = 0;                 // 0: bf16 x; 1: rmsnorm of h_in
-    const float *h_in = nullptr;    // [M][ld_h_in] f32
-    int64_t ld_h_in = 0;
-    const float *ss_in = nullptr;   // [ss_tiles][16] f32 sums of squares of h_in rows
-    int ss_tiles = 0;
-    const uint16_t *gamma = nullptr;  // [K] bf16
-    float eps = 1e-5f;
+    int x_mode = 0;                 // 0: natural bf16 x; 1: x already in the kernel's order
     int epi = EPI_STORE;
     float *h_out = nullptr;         // EPI_RESID: [M][ld_h_out] f32, updated in place
     int64_t ld_h_out = 0;
     float *ss_out = nullptr;        // EPI_RESID: [N/16][16] f32
     uint16_t *act = nullptr;        // EPI_SILU_MUL: [M][ld_act] bf16, N/2 columns
     int64_t ld_act = 0;
+    int act_pair_order = 0;         // EPI_SILU_MUL: write act in the 4-bit pair order
     unsigned long long *amax = nullptr;  // EPI_ARGMAX: [M]
 };
 bool qmv_supported(const QmmArgs &a, const char **why);
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes);
 size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p);
+// Bytes at the end of the qmv workspace that hold pair-ordered x (4-bit, x_mode 0).
+size_t qmv_prep_bytes(const QmmArgs &a);
+// Activations into the qmv's order (4-bit: pair order [x0 x4 x1 x5 x2 x6 x3 x7]
+// within every 8 columns; 8-bit: natural), bf16 [M][ld_dst].  mode 0: src is
+// bf16 [M][ld_src]; mode 1: src is the f32 residual stream h, normalised with
+// the per-16-column partial sums of squares ss ([ss_tiles][16]) and gamma.
+cudaError_t launch_qmv_prep(const void *src, int64_t ld_src, int mode, const float *ss, int ss_tiles,
+                            const uint16_t *gamma, float eps, int M, int K, int bits, uint16_t *dst, int64_t ld_dst,
+                            cudaStream_t stream);
 cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &p, void *workspace, cudaStream_t stream,
                        const QmvFusion *fusion = nullptr);
 
@@ -84,6 +90,7 @@ struct DecodeAttnArgs {
     int64_t ld_out;
     int batch, q_heads, kv_heads, head_dim, capacity;
     float scale;
+    int out_pair_order;             // write out in the 4-bit qmv pair order
 };
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, cudaStream_t stream);
 cudaError_t launch_embed(const void *table, int64_t ld_table, const int *tokens, int B, int D, float *h, float *ss_out,

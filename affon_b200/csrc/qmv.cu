@@ -3,40 +3,51 @@
 // activations / scales / biases, f32 accumulation (the layout and formula of
 // docs/core/quantized-inference.md:45-67).
 //
-// Streaming.  Persistent CTAs, one per SM.  One producer warp moves the
-// packed weight matrix through a ring of shared-memory stages with 2D TMA
-// loads (ROWS rows x 128 bytes per stage, 128-byte swizzle, plus the matching
-// ROWS x 8 boxes of bf16 scales and biases), so ~120 KB per SM are in flight
-// without costing registers.  Consumer warps read the packed words from
-// shared memory, decode them in registers and feed tensor cores.
+// Streaming.  Persistent CTAs, one per SM.  One producer warp moves each
+// 256-row x 128-byte stage of the packed weight matrix through a ring of
+// shared-memory stages with 2D TMA loads (128-byte swizzle), together with the
+// matching 256 x 8 boxes of bf16 scales and biases and the stage's activation
+// columns (16 rows x 64 columns per group, 128-byte swizzle).  The ring holds
+// ~190 KB per SM in flight without costing registers, and the activations
+// need no separate staging pass.  Sixteen consumer warps (one 16-row weight
+// tile each) decode the packed words in registers and feed tensor cores.
 //
-// Why tensor cores at M <= 16: at ~6.5 TB/s a 4-bit weight stream delivers
-// ~11.6e12 weights/s; decoding each weight to a float and multiplying it on
-// the CUDA cores costs ~3 lane-ops, as much as the 148 SMs can issue.  The
-// decoded codes go straight from registers into the A fragments of
+// Why mma.sync tensor cores at M <= 16: at ~6.5 TB/s a 4-bit weight stream
+// delivers ~13e12 weights/s; decoding each weight to a float and multiplying
+// it on the CUDA cores costs ~3 lane-ops, as much as the 148 SMs can issue.
+// The decoded codes go straight from registers into the A fragments of
 // m16n8k16 bf16 MMAs (weights as the 16-row A operand, activations as B).
+// tcgen05 MMAs do not fit this shape: each instruction occupies the SM's
+// tensor core for ~146 cycles whatever its N (16..256), so at N <= 16 the
+// 128 x 16 weights per instruction cap a CTA near 7 bytes of codes per cycle.
 // Shifts of the nibble decoder are issued as mul.hi so they run on the FMA
 // pipe beside the logic ops on the ALU pipe.
 //
 // Exact codes, per-group affine in f32: the MMA multiplies the integer codes
 // (4-bit: as 128+q, exact in bf16) by x, giving C_g = sum_{k in g} x*code in
-// f32; the affine decode is applied per group of 64 outside the tensor core:
-//     y += s[n,g] * C_g + (b[n,g] - 128 s[n,g]) * X_g,  X_g = sum_{k in g} x[k]
-// evaluated as fused multiply-adds so the offset terms cancel exactly.  This
-// is sum_k x*(s*q+b) up to reassociation; weights are never rounded to bf16
-// (quantized-inference.md:119-121).  Numerical class: reassociated.
+// f32.  The activation sums X_g = sum_{k in g} x[k] are the same for every
+// weight row: one "sum" warp per CTA computes them once per stage (MMAs with
+// an all-ones A operand) into shared memory.  The affine decode is applied per
+// group of 64 outside the tensor core:
+//     y += s[n,g] * C_g + (b[n,g] - 128 s[n,g]) * X_g
+// with packed f32x2 fused multiply-adds, so the offset terms cancel exactly.
+// This is sum_k x*(s*q+b) up to reassociation; weights are never rounded to
+// bf16 (quantized-inference.md:119-121).  Numerical class: reassociated.
 //
-// Work partition (stream-K).  The work is a flat list of items
-// (K split, 16*NT*CW-row block, 128-byte K stage), split-major.  CTA c takes
-// the items [c*T/C, (c+1)*T/C), so every CTA streams the same number of
-// bytes.  K is split where x would not fit in shared memory and, beyond that,
-// where staging x in every CTA would cost more on-chip traffic than the extra
-// partial sums; a CTA restages x when its range enters a new split.  A block
-// that lies inside one CTA and one split is stored directly; a block shared
-// by several CTAs or splits is combined through f32 partials: each
-// contributing CTA writes its slot, and the CTA arriving last (per-block
-// counter) sums the slots in a fixed order and stores y, so results do not
-// depend on scheduling.  That CTA resets the counter for the next launch.
+// Activation layout.  For 4-bit codes the kernel reads x in "pair order":
+// within every 8 consecutive columns the order is [x0 x4 x1 x5 x2 x6 x3 x7],
+// matching the (q_p, q_{p+4}) pairs one logic op extracts from a packed word.
+// launch_qmv_prep writes that order from natural bf16 x (and, for the decoder,
+// the RMS-normalised residual stream); 8-bit codes use natural order.
+//
+// Work partition (stream-K).  The work is a flat list of items (256-row
+// block, 128-byte K stage).  CTA c takes the items [c*T/C, (c+1)*T/C), so
+// every CTA streams the same number of bytes.  A block that lies inside one
+// CTA is stored directly; a block shared by several CTAs is combined through
+// f32 partials: each contributing CTA writes its slot, and the CTA arriving
+// last (per-block counter) sums the slots in a fixed order and stores y, so
+// results do not depend on scheduling.  That CTA resets the counter for the
+// next launch.
 #include <algorithm>
 #include <cmath>
 
@@ -48,35 +59,32 @@ namespace afb {
 namespace qmv {
 
 constexpr int GROUP = 64;
-constexpr int XS_PAD = 8;
 constexpr int MAX_STAGES = 8;
-
-template <int NT, int CW>
-struct Geom {
-    static constexpr int ROWS = 16 * NT * CW;   // rows per block (= TMA box height)
-    static constexpr int W_BYTES = ROWS * 128;  // packed bytes per stage
-    static constexpr int SB_BYTES = ROWS * 16;  // one 8-group box of scales (or biases)
-    static constexpr int STAGE_BYTES = W_BYTES + 2 * SB_BYTES;
-};
+constexpr int X_BOX_BYTES = 16 * 128;  // one group of activation columns: 16 rows x 64 bf16
+constexpr int CONSUMERS = 16;          // consumer warps: one 16-row weight tile each, 256-row blocks
+constexpr int NT = 1;                  // 16-row weight tiles per consumer warp
+constexpr int ROWS = 16 * NT * CONSUMERS;
+constexpr int THREADS = 32 * (CONSUMERS + 2);  // consumers, producer, sum warp
 
 template <int BITS>
 struct Shape {
     static constexpr int GPS = BITS == 4 ? 4 : 2;  // groups per stage (128 packed bytes per row)
     static constexpr int KPS = GPS * GROUP;         // K per stage
+    static constexpr int W = ROWS * 128;            // packed bytes per stage
+    static constexpr int SB = ROWS * 16;            // one 8-group box of scales (or biases)
+    static constexpr int X = GPS * X_BOX_BYTES;
+    static constexpr int BYTES = W + 2 * SB + X;    // all offsets stay 1024-byte aligned
 };
 
 struct Params {
-    const uint16_t *x;
-    int64_t ldx;
     void *y;
     int64_t ldy;
     float *partial;
     unsigned *counters;
     unsigned *status;
     int M, N, K;
-    int splits, ks;       // K splits (x slices that fit shared memory) and K per split
-    int nblocks, spb;     // blocks along N and stages per block per split
-    int64_t items;        // splits * nblocks * spb
+    int nblocks, spb;     // blocks along N and stages per block
+    int64_t items;        // nblocks * spb
     int stages;           // ring depth
     int max_slots;        // partial slots per block
     int y_bf16;
@@ -99,6 +107,16 @@ __device__ __forceinline__ uint32_t dec8(uint32_t w, int i) {
     return pack_bf16x2(f0, f1);
 }
 
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+// d = a * b + c on packed f32 pairs (one instruction, sm_100a).
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 __device__ __forceinline__ void store_out(const Params &p, int m, int64_t n, float v) {
     if (p.y_bf16)
         static_cast<uint16_t *>(p.y)[m * p.ldy + n] = f32_to_bf16_bits(v);
@@ -106,32 +124,18 @@ __device__ __forceinline__ void store_out(const Params &p, int m, int64_t n, flo
         static_cast<float *>(p.y)[m * p.ldy + n] = v;
 }
 
-__device__ __forceinline__ const float *base_of_slot(const float *base, int slot, int M, int rows) {
-    return base + static_cast<int64_t>(slot) * M * rows;
-}
-
 // Owner CTA of flat item i when CTA c holds [floor(c*T/C), floor((c+1)*T/C)).
 __device__ __forceinline__ int owner_of(int64_t i, int64_t T, int C) {
     return static_cast<int>(((i + 1) * C - 1) / T);
-}
-
-// Contributor count of block blk (all splits) and the slot of CTA c for split.
-__device__ __forceinline__ void contributors(const Params &p, int split, int blk, int c, int C, int &total,
-                                             int &slot) {
-    total = 0;
-    slot = -1;
-    for (int s = 0; s < p.splits; ++s) {
-        const int64_t b0 = (static_cast<int64_t>(s) * p.nblocks + blk) * p.spb;
-        const int first = owner_of(b0, p.items, C), last = owner_of(b0 + p.spb - 1, p.items, C);
-        if (s == split) slot = total + (c - first);
-        total += last - first + 1;
-    }
 }
 
 __device__ __forceinline__ uint32_t f32_order_key(float v) {
     const uint32_t u = __float_as_uint(v);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+
+// Pair-order slot of column e (0..7) within its 8 columns: 0 4 1 5 2 6 3 7.
+__device__ __forceinline__ int pair_slot(int e) { return (e < 4) ? 2 * e : 2 * (e - 4) + 1; }
 
 // Apply the epilogue to the row pair (n_lo, n_lo + 8) of activation row m.
 // Returns the contribution of this pair to the per-tile reductions:
@@ -151,7 +155,10 @@ __device__ __forceinline__ unsigned long long epilogue_pair(const Params &p, int
     }
     case EPI_SILU_MUL:
         if (ok_hi) {  // tile rows 0-7 are gate rows, 8-15 the matching up rows
-            const int64_t j = (n_lo >> 4) * 8 + (n_lo & 7);
+            // act column j = 8*(n/16) + n%8, at its pair-order slot when the
+            // consumer is a 4-bit qmv
+            const int e = static_cast<int>(n_lo & 7);
+            const int64_t j = (n_lo >> 4) * 8 + (p.f.act_pair_order ? pair_slot(e) : e);
             const float gate = v_lo;
             const float silu = gate / (1.0f + __expf(-gate));
             p.f.act[m * p.f.ld_act + j] = f32_to_bf16_bits(silu * v_hi);
@@ -209,191 +216,150 @@ __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT
         }
 }
 
-// Epilogue of one (split, block) segment of this CTA for the warp's NT tiles.
-// Called by all consumer warps together.  `flag` is a shared-memory word.
-template <int MT, int NT, int CW>
-__device__ __forceinline__ void segment_epilogue(const Params &p, float (&acc)[NT][MT][4], int split, int blk, int warp,
+// Final value v of weight row n for activation row m, one thread per row,
+// 32 consecutive rows per warp (a 16-row tile is one half warp; rows n and
+// n+8 sit in lanes l and l+8).  Called by all 32 lanes with the same m.
+__device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, float v, int lane) {
+    const bool ok = n < p.N;
+    switch (p.f.epi) {
+    case EPI_RESID: {
+        float hv = 0.0f;
+        if (ok) {
+            float *h = p.f.h_out + m * p.f.ld_h_out + n;
+            hv = *h + v;
+            *h = hv;
+        }
+        float ssq = hv * hv;
+        ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
+        ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
+        ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
+        ssq += __shfl_xor_sync(0xffffffffu, ssq, 8);
+        if (ok && (lane & 15) == 0) p.f.ss_out[(n >> 4) * 16 + m] = ssq;
+        break;
+    }
+    case EPI_SILU_MUL: {
+        const float up = __shfl_down_sync(0xffffffffu, v, 8);
+        if ((lane & 8) == 0 && n + 8 < p.N) {
+            const int e = static_cast<int>(n & 7);
+            const float silu = v / (1.0f + __expf(-v));
+            p.f.act[m * p.f.ld_act + (n >> 4) * 8 + (p.f.act_pair_order ? pair_slot(e) : e)] =
+                f32_to_bf16_bits(silu * up);
+        }
+        break;
+    }
+    case EPI_ARGMAX: {
+        unsigned long long best =
+            ok ? (static_cast<unsigned long long>(f32_order_key(v)) << 32) | (0xFFFFFFFFu - uint32_t(n)) : 0ull;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane == 0 && best) atomicMax(&p.f.amax[m], best);
+        break;
+    }
+    default:
+        if (ok) store_out(p, m, n, v);
+    }
+}
+
+// Epilogue of one block segment of this CTA, called by all consumer warps
+// together.  `flag` is a shared-memory word.
+template <int MT>
+__device__ __forceinline__ void segment_epilogue(const Params &p, const float (&acc)[MT][4], int blk, int warp,
                                                  int g, int t, int lane, int tid, volatile int *flag) {
-    constexpr int ROWS = Geom<NT, CW>::ROWS;
-    int total, slot;
-    contributors(p, split, blk, blockIdx.x, gridDim.x, total, slot);
+    constexpr int CT = CONSUMERS * 32;  // consumer threads
+    const int64_t b0 = static_cast<int64_t>(blk) * p.spb;
+    const int first = owner_of(b0, p.items, gridDim.x), last_owner = owner_of(b0 + p.spb - 1, p.items, gridDim.x);
+    const int total = last_owner - first + 1;
     const int64_t nb0 = static_cast<int64_t>(blk) * ROWS;
     if (total == 1) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) finish_tile<MT>(p, acc[nt], nb0 + (warp * NT + nt) * 16, g, t);
+        finish_tile<MT>(p, acc, nb0 + warp * 16, g, t);
         return;
     }
+    const int slot = static_cast<int>(blockIdx.x) - first;
     // partial[((blk * max_slots + slot) * M + m) * ROWS + row]
-    float *base = p.partial + (static_cast<int64_t>(blk) * p.max_slots) * p.M * ROWS;
-    float *const base_ptr = base;
+    float *base = p.partial + static_cast<int64_t>(blk) * p.max_slots * p.M * ROWS;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int m = 2 * t + 8 * mt + (i & 1);
-                const int r = (warp * NT + nt) * 16 + g + 8 * (i >> 1);
-                if (m < p.M) base[(static_cast<int64_t>(slot) * p.M + m) * ROWS + r] = acc[nt][mt][i];
-            }
+        for (int i = 0; i < 4; ++i) {
+            const int m = 2 * t + 8 * mt + (i & 1);
+            const int r = warp * 16 + g + 8 * (i >> 1);
+            if (m < p.M) base[(static_cast<int64_t>(slot) * p.M + m) * ROWS + r] = acc[mt][i];
+        }
     // Message passing through the per-block counter (one arrival per
     // contributing CTA): every thread releases its partials with a gpu-scope
     // acq_rel fence, the consumer warps meet, one thread takes the ticket,
     // and in the last contributor every thread fences again before reading
     // all slots.
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    named_bar_sync(1, CW * 32);
+    named_bar_sync(1, CT);
     if (tid == 0) *flag = (atomicAdd(&p.counters[blk], 1u) == static_cast<unsigned>(total - 1)) ? 1 : 0;
-    named_bar_sync(1, CW * 32);
-    const bool last = *flag != 0;
-    named_bar_sync(1, CW * 32);  // the flag is reused by the next segment
-    if (!last) return;
+    named_bar_sync(1, CT);
+    const bool is_last = *flag != 0;
+    named_bar_sync(1, CT);  // the flag is reused by the next segment
+    if (!is_last) return;
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    // Each warp reduces the rows it owns, lanes over (row, row+8) pairs of its
-    // tiles so the pair epilogues and per-tile reductions apply unchanged.
-    for (int base = warp * 8 * NT; base < (warp + 1) * 8 * NT; base += 32) {
-        const int pr = base + lane;
-        const bool active = pr < (warp + 1) * 8 * NT;
-        const int r_lo = (pr >> 3) * 16 + (pr & 7);
-        for (int m = 0; m < p.M; ++m) {
-            float ssq = 0.0f;
-            unsigned long long best = 0ull;
-            if (active) {
-                float lo = 0.0f, hi = 0.0f;
-                for (int sl = 0; sl < total; ++sl) {
-                    const float *slot_base = base_of_slot(base_ptr, sl, p.M, ROWS) + static_cast<int64_t>(m) * ROWS;
-                    lo += __ldcg(&slot_base[r_lo]);
-                    hi += __ldcg(&slot_base[r_lo + 8]);
-                }
-                best = epilogue_pair(p, m, nb0 + r_lo, lo, hi, ssq);
-            }
-            // lanes pr..pr+7 share a tile: reduce over the low 3 lane bits
-            if (p.f.epi == EPI_RESID) {
-                ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
-                ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
-                ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
-                if (active && (pr & 7) == 0) p.f.ss_out[((nb0 + r_lo) >> 4) * 16 + m] = ssq;
-            } else if (p.f.epi == EPI_ARGMAX) {
+    // The last contributor sums the slots in slot order.  Thread = (block
+    // row, parity of m); all loads of a batch of slots are issued before the
+    // ordered adds, so the combine costs a few L2 round trips.
+    constexpr int TPR = CT / ROWS;  // threads per block row
+    static_assert(TPR * ROWS == CT && (TPR == 1 || TPR == 2), "combine thread map");
+    constexpr int MH = (MT * 8 + TPR - 1) / TPR;  // activation rows per thread
+    constexpr int BATCH = 4;
+    const int row = tid % ROWS, m0 = tid / ROWS;
+    float v[MH];
 #pragma unroll
-                for (int o = 1; o < 8; o <<= 1) {
-                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-                    best = other > best ? other : best;
-                }
-                if (active && (pr & 7) == 0 && best) atomicMax(&p.f.amax[m], best);
-            }
+    for (int j = 0; j < MH; ++j) v[j] = 0.0f;
+    for (int sl0 = 0; sl0 < total; sl0 += BATCH) {
+        float tmp[MH][BATCH];
+#pragma unroll
+        for (int j = 0; j < MH; ++j) {
+            const int m = m0 + TPR * j;
+#pragma unroll
+            for (int u = 0; u < BATCH; ++u)
+                tmp[j][u] = (m < p.M && sl0 + u < total)
+                                ? __ldcg(base + (static_cast<int64_t>(sl0 + u) * p.M + m) * ROWS + row)
+                                : 0.0f;
         }
+#pragma unroll
+        for (int j = 0; j < MH; ++j)
+#pragma unroll
+            for (int u = 0; u < BATCH; ++u) v[j] += tmp[j][u];
+    }
+#pragma unroll
+    for (int j = 0; j < MH; ++j) {
+        const int m = m0 + TPR * j;
+        if (m >= p.M) break;  // warp-uniform
+        finish_row(p, m, nb0 + row, v[j], lane);
     }
     if (tid == 0) atomicExch(&p.counters[blk], 0u);
 }
 
-// Stage x[:, k0:k0+ks) (and the group sums X_g) into shared memory; run by
-// the consumer warps only.
-template <int BITS>
-__device__ __forceinline__ void stage_x(const Params &p, char *xs, float *xg, int xs_rs, int64_t k0, int tid,
-                                        int nthreads, float *rms, float *red) {
-    const int gs = p.ks / GROUP;
-    for (int i = tid; i < gs * 16; i += nthreads) xg[i] = 0.0f;
-    if (p.f.x_mode == 1) {
-        // 1/rms of every activation row from the per-tile sums of squares
-        // (fixed summation order: per thread, then per warp, then per CTA).
-        float acc[16];
-#pragma unroll
-        for (int m = 0; m < 16; ++m) acc[m] = 0.0f;
-        for (int tl = tid; tl < p.f.ss_tiles; tl += nthreads) {
-            const float4 *src = reinterpret_cast<const float4 *>(p.f.ss_in + static_cast<int64_t>(tl) * 16);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 v = __ldcg(src + q);
-                acc[4 * q] += v.x; acc[4 * q + 1] += v.y; acc[4 * q + 2] += v.z; acc[4 * q + 3] += v.w;
-            }
-        }
-        const int lane = tid & 31, w = tid >> 5;
-#pragma unroll
-        for (int m = 0; m < 16; ++m) {
-#pragma unroll
-            for (int o = 16; o; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-            if (lane == 0) red[w * 16 + m] = acc[m];
-        }
-        named_bar_sync(1, nthreads);
-        if (tid < 16) {
-            float sum = 0.0f;
-            for (int ww = 0; ww < nthreads / 32; ++ww) sum += red[ww * 16 + tid];
-            rms[tid] = rsqrtf(sum / static_cast<float>(p.K) + p.f.eps);
-        }
-    }
-    named_bar_sync(1, nthreads);
-    const int cpr = p.ks / 8;  // 16-byte chunks per row
-    const int total = p.M * cpr;
-    for (int base = 0; base < total; base += nthreads) {
-        const int c = base + tid;
-        const bool valid = c < total;
-        const int m = valid ? c / cpr : 0, kc = valid ? c % cpr : 0;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid) {
-            if (p.f.x_mode == 1) {  // x = bf16(h * rms * gamma)
-                const float4 *hp = reinterpret_cast<const float4 *>(p.f.h_in + m * p.f.ld_h_in + k0 + kc * 8);
-                const float4 h0 = __ldcg(hp), h1 = __ldcg(hp + 1);
-                const uint4 gm = ldg_nc_v4(p.f.gamma + k0 + kc * 8);
-                const float r = rms[m];
-                auto nb = [&](float hv, uint32_t gw, int hi) {
-                    return f32_to_bf16_bits(hv * r * bf16_bits_to_f32(hi ? (gw >> 16) : (gw & 0xFFFF)));
-                };
-                v.x = nb(h0.x, gm.x, 0) | (uint32_t(nb(h0.y, gm.x, 1)) << 16);
-                v.y = nb(h0.z, gm.y, 0) | (uint32_t(nb(h0.w, gm.y, 1)) << 16);
-                v.z = nb(h1.x, gm.z, 0) | (uint32_t(nb(h1.y, gm.z, 1)) << 16);
-                v.w = nb(h1.z, gm.w, 0) | (uint32_t(nb(h1.w, gm.w, 1)) << 16);
-            } else {
-                v = ldg_nc_v4(p.x + m * p.ldx + k0 + kc * 8);
-            }
-        }
-        float sum = bf16_bits_to_f32(v.x & 0xFFFF) + bf16_bits_to_f32(v.x >> 16) + bf16_bits_to_f32(v.y & 0xFFFF) +
-                    bf16_bits_to_f32(v.y >> 16) + bf16_bits_to_f32(v.z & 0xFFFF) + bf16_bits_to_f32(v.z >> 16) +
-                    bf16_bits_to_f32(v.w & 0xFFFF) + bf16_bits_to_f32(v.w >> 16);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        if (valid) {
-            if constexpr (BITS == 4) {  // [x0 x4 x1 x5 x2 x6 x3 x7] matches dec4's pairs
-                uint4 o;
-                o.x = prmt(v.x, v.z, 0x5410u);
-                o.y = prmt(v.x, v.z, 0x7632u);
-                o.z = prmt(v.y, v.w, 0x5410u);
-                o.w = prmt(v.y, v.w, 0x7632u);
-                v = o;
-            }
-            *reinterpret_cast<uint4 *>(xs + m * xs_rs + kc * 16) = v;
-            if ((kc & 7) == 0) xg[(kc >> 3) * 16 + m] = sum;
-        }
-    }
-    named_bar_sync(1, nthreads);
-}
-
-template <int BITS, int MT, int NT, int CW>
-__global__ void __launch_bounds__(32 * (CW + 1), 1)
+template <int BITS, int MT>
+__global__ void __launch_bounds__(THREADS, 1)
     qmv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
-               const __grid_constant__ CUtensorMap bmap, Params p) {
-    using Gm = Geom<NT, CW>;
-    constexpr int STAGE_BYTES = Gm::STAGE_BYTES, W_BYTES = Gm::W_BYTES, SB_BYTES = Gm::SB_BYTES, ROWS = Gm::ROWS;
-    constexpr int GPS = Shape<BITS>::GPS, KPS = Shape<BITS>::KPS;
+               const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap xmap, Params p) {
+    using Sh = Shape<BITS>;
+    constexpr int GPS = Sh::GPS, KPS = Sh::KPS, CW = CONSUMERS;
     extern __shared__ char smem_raw[];
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
     char *ring = smem;
-    const int xs_rs = (p.ks + XS_PAD) * 2;
-    char *xs = ring + S * STAGE_BYTES;
-    float *xg = reinterpret_cast<float *>(xs + p.M * xs_rs);
-    uint64_t *full = reinterpret_cast<uint64_t *>(xg + (p.ks / GROUP) * 16);
+    float *xsums = reinterpret_cast<float *>(ring + S * Sh::BYTES);  // [stage][group][16]
+    uint64_t *full = reinterpret_cast<uint64_t *>(xsums + MAX_STAGES * GPS * 16);
     uint64_t *empty = full + MAX_STAGES;
-    volatile int *abort = reinterpret_cast<volatile int *>(empty + MAX_STAGES);
+    uint64_t *xsfull = empty + MAX_STAGES;
+    volatile int *abort = reinterpret_cast<volatile int *>(xsfull + MAX_STAGES);
     volatile int *flag = abort + 1;
-    float *rms = reinterpret_cast<float *>(empty + MAX_STAGES) + 4;  // [16]
-    float *red = rms + 16;                                            // [CW][16]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], CW);
+            mbar_init(&empty[s], CW + 1);  // consumer warps and the sum warp
+            mbar_init(&xsfull[s], 1);
         }
         *abort = 0;
         fence_mbar_init();
@@ -403,120 +369,171 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
     const int64_t T = p.items;
     const int64_t lo = static_cast<int64_t>(blockIdx.x) * T / gridDim.x;
     const int64_t hi = static_cast<int64_t>(blockIdx.x + 1) * T / gridDim.x;
-    const int64_t per_split = static_cast<int64_t>(p.nblocks) * p.spb;
+    const int g = lane >> 2, t = lane & 3;
 
     if (warp == CW) {  // ------------------------------------------ producer
         if (lane == 0) {
             tma_prefetch_desc(&wmap);
             tma_prefetch_desc(&smap);
             tma_prefetch_desc(&bmap);
+            tma_prefetch_desc(&xmap);
             int stage = 0;
-            uint32_t phase = 0;
+            uint32_t phase = 0, issued_mask = 0, issued_par = 0;
             for (int64_t i = lo; i < hi; ++i) {
-                const int split = static_cast<int>(i / per_split);
-                const int64_t rem = i - split * per_split;
-                const int blk = static_cast<int>(rem / p.spb), st = static_cast<int>(rem - int64_t(blk) * p.spb);
-                // On a timed-out wait (abort set) stop issuing loads; consumers drain.
-                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) return;
-                char *dst = ring + stage * STAGE_BYTES;
-                mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-                const int64_t kk = static_cast<int64_t>(split) * p.ks + static_cast<int64_t>(st) * KPS;
-                tma_load_2d(dst, &wmap, &full[stage], static_cast<int>(kk * BITS / 32), blk * ROWS);
-                const int g8 = static_cast<int>((kk / GROUP) & ~int64_t(7));
-                tma_load_2d(dst + W_BYTES, &smap, &full[stage], g8, blk * ROWS);
-                tma_load_2d(dst + W_BYTES + SB_BYTES, &bmap, &full[stage], g8, blk * ROWS);
+                const int blk = static_cast<int>(i / p.spb), st = static_cast<int>(i - int64_t(blk) * p.spb);
+                // On a timed-out wait (abort set) stop issuing loads; the other
+                // roles walk to the end without waiting.
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) break;
+                char *dst = ring + stage * Sh::BYTES;
+                mbar_arrive_expect_tx(&full[stage], Sh::BYTES);
+                const int kk = st * KPS;
+                tma_load_2d(dst, &wmap, &full[stage], kk * BITS / 32, blk * ROWS);
+                const int g8 = (kk / GROUP) & ~7;
+                tma_load_2d(dst + Sh::W, &smap, &full[stage], g8, blk * ROWS);
+                tma_load_2d(dst + Sh::W + Sh::SB, &bmap, &full[stage], g8, blk * ROWS);
+#pragma unroll
+                for (int G = 0; G < GPS; ++G)
+                    tma_load_2d(dst + Sh::W + 2 * Sh::SB + G * X_BOX_BYTES, &xmap, &full[stage], kk + G * GROUP, 0);
+                issued_mask |= 1u << stage;
+                issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
                 if (++stage == S) { stage = 0; phase ^= 1; }
             }
+            // Let every copy this CTA issued land before the CTA exits.
+            for (int s = 0; s < S; ++s)
+                if (issued_mask & (1u << s)) mbar_wait_drain(&full[s], (issued_par >> s) & 1u);
         }
-        return;
-    }
-
-    // ------------------------------------------------------------ consumers
-    const int g = lane >> 2, t = lane & 3;
-    int stage = 0;
-    uint32_t phase = 0;
-    int cur_split = -1;
-    int64_t i = lo;
-    while (i < hi) {
-        const int split = static_cast<int>(i / per_split);
-        const int64_t rem = i - split * per_split;
-        const int blk = static_cast<int>(rem / p.spb);
-        const int64_t blk_begin = static_cast<int64_t>(split) * per_split + static_cast<int64_t>(blk) * p.spb;
-        const int64_t seg_end = min(hi, blk_begin + p.spb);
-        if (split != cur_split) {
-            named_bar_sync(1, CW * 32);
-            stage_x<BITS>(p, xs, xg, xs_rs, static_cast<int64_t>(split) * p.ks, tid, CW * 32, rms, red);
-            cur_split = split;
-        }
-        float acc[NT][MT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) acc[nt][mt][0] = acc[nt][mt][1] = acc[nt][mt][2] = acc[nt][mt][3] = 0.f;
-
-        for (; i < seg_end; ++i) {
-            const int j = static_cast<int>(i - blk_begin);  // stage index within the block
-            // A timed-out wait sets *abort; keep walking the loop (results are
-            // then garbage and the status word says TIMEOUT) so that every
-            // consumer reaches the same named barriers and no thread hangs.
+        __syncwarp();
+    } else if (warp == CW + 1) {  // ----------------------------- group sums
+        // X_g = sum_{k in g} x[m][k] for every activation row, once per CTA and
+        // stage, via m16n8k16 MMAs with an all-ones A operand (rows equal).
+        const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 1.0 pairs
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int64_t i = lo; i < hi; ++i) {
             mbar_wait(&full[stage], phase, abort, p.status);
-            const char *sw = ring + stage * STAGE_BYTES;
-            const char *ssb = sw + W_BYTES;
-            const char *bsb = ssb + SB_BYTES;
-            const int go0 = (j * GPS) & 7;  // first group of this stage within the 8-group scale box
-            uint32_t sv[NT][2][GPS / 2], bv[NT][2][GPS / 2];
+            const char *xsb = ring + stage * Sh::BYTES + Sh::W + 2 * Sh::SB;
+            float *xs = xsums + stage * GPS * 16;
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int r = (warp * NT + nt) * 16 + g + 8 * h;
-                    if constexpr (GPS == 4) {
-                        const uint2 a = *reinterpret_cast<const uint2 *>(ssb + r * 16 + go0 * 2);
-                        const uint2 b = *reinterpret_cast<const uint2 *>(bsb + r * 16 + go0 * 2);
-                        sv[nt][h][0] = a.x; sv[nt][h][1] = a.y; bv[nt][h][0] = b.x; bv[nt][h][1] = b.y;
-                    } else {
-                        sv[nt][h][0] = *reinterpret_cast<const uint32_t *>(ssb + r * 16 + go0 * 2);
-                        bv[nt][h][0] = *reinterpret_cast<const uint32_t *>(bsb + r * 16 + go0 * 2);
-                    }
-                }
-#pragma unroll
-            for (int G = 0; G < GPS; ++G) {
-                const int Gl = j * GPS + G;  // group index within the split
-                uint32_t xf[MT][8];
-                float2 X[MT];
+            for (int G = 0; G < GPS; ++G)
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
-                    const int m = g + 8 * mt;
-                    if (m < p.M) {
-                        const char *src = xs + m * xs_rs + (Gl * GROUP + 16 * t) * 2;
-                        const uint4 v0 = *reinterpret_cast<const uint4 *>(src);
-                        const uint4 v1 = *reinterpret_cast<const uint4 *>(src + 16);
+                    const char *row = xsb + G * X_BOX_BYTES + (g + 8 * mt) * 128;
+                    const uint4 v0 = *reinterpret_cast<const uint4 *>(row + (((2 * t) ^ g) << 4));
+                    const uint4 v1 = *reinterpret_cast<const uint4 *>(row + (((2 * t + 1) ^ g) << 4));
+                    float cx[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma_bf16_16816(cx, ones, v0.x, v0.y, cx);
+                    mma_bf16_16816(cx, ones, v0.z, v0.w, cx);
+                    mma_bf16_16816(cx, ones, v1.x, v1.y, cx);
+                    mma_bf16_16816(cx, ones, v1.z, v1.w, cx);
+                    if (g == 0) {  // cx[0], cx[1] = X of activation rows 2t, 2t+1 (+8 mt)
+                        xs[G * 16 + 8 * mt + 2 * t] = cx[0];
+                        xs[G * 16 + 8 * mt + 2 * t + 1] = cx[1];
+                    }
+                }
+            fence_proxy_async_smem();  // x reads before the stage's next TMA fill
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&xsfull[stage]);
+                mbar_arrive(&empty[stage]);
+            }
+            if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+    } else {  // ------------------------------------------------- consumers
+        int stage = 0;
+        uint32_t phase = 0;
+        int64_t i = lo;
+        const int r0 = warp * 16 + g;  // block rows r0 and r0 + 8 of this thread
+        while (i < hi) {
+            const int blk = static_cast<int>(i / p.spb);
+            const int64_t blk_begin = static_cast<int64_t>(blk) * p.spb;
+            const int64_t seg_end = min(hi, blk_begin + p.spb);
+            uint64_t acc[MT][2];  // packed f32 pairs: [mt][0] = (c0, c1), [mt][1] = (c2, c3)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = 0ull;
+
+            for (; i < seg_end; ++i) {
+                const int j = static_cast<int>(i - blk_begin);  // stage index within the block
+                // A timed-out wait sets *abort; keep walking the loop (results are
+                // then garbage and the status word says TIMEOUT) so that every
+                // consumer reaches the same barriers and no thread hangs.
+                mbar_wait(&full[stage], phase, abort, p.status);
+                const char *sw = ring + stage * Sh::BYTES;
+                const char *ssb = sw + Sh::W;
+                const char *bsb = ssb + Sh::SB;
+                const char *xsb = bsb + Sh::SB;
+                const int go0 = (j * GPS) & 7;  // first group of this stage within the 8-group scale box
+                uint32_t sv[2][GPS / 2], bv[2][GPS / 2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int r = r0 + 8 * h;
+                    if constexpr (GPS == 4) {
+                        const uint2 a2 = *reinterpret_cast<const uint2 *>(ssb + r * 16 + go0 * 2);
+                        const uint2 b2 = *reinterpret_cast<const uint2 *>(bsb + r * 16 + go0 * 2);
+                        sv[h][0] = a2.x; sv[h][1] = a2.y; bv[h][0] = b2.x; bv[h][1] = b2.y;
+                    } else {
+                        sv[h][0] = *reinterpret_cast<const uint32_t *>(ssb + r * 16 + go0 * 2);
+                        bv[h][0] = *reinterpret_cast<const uint32_t *>(bsb + r * 16 + go0 * 2);
+                    }
+                }
+                mbar_wait(&xsfull[stage], phase, abort, p.status);
+                const float *xs = xsums + stage * GPS * 16;
+#pragma unroll
+                for (int G = 0; G < GPS; ++G) {
+                    // B fragments: row m = g + 8*mt of the group's 16 x 64 box,
+                    // columns 16t..16t+15 = 16-byte chunks 2t, 2t+1 stored at
+                    // chunk ^ (m % 8) (128-byte swizzle).
+                    uint32_t xf[MT][8];
+                    const char *xb = xsb + G * X_BOX_BYTES;
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        const char *row = xb + (g + 8 * mt) * 128;
+                        const uint4 v0 = *reinterpret_cast<const uint4 *>(row + (((2 * t) ^ g) << 4));
+                        const uint4 v1 = *reinterpret_cast<const uint4 *>(row + (((2 * t + 1) ^ g) << 4));
                         xf[mt][0] = v0.x; xf[mt][1] = v0.y; xf[mt][2] = v0.z; xf[mt][3] = v0.w;
                         xf[mt][4] = v1.x; xf[mt][5] = v1.y; xf[mt][6] = v1.z; xf[mt][7] = v1.w;
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) xf[mt][e] = 0u;
                     }
-                    X[mt] = *reinterpret_cast<const float2 *>(xg + Gl * 16 + 2 * t + 8 * mt);
-                }
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    const int r0 = (warp * NT + nt) * 16 + g;  // block row of this thread (and r0 + 8)
-                    uint32_t w0[4], w1[4];
+                    // A fragments of all four k-steps first, then the MMAs with
+                    // the m-tiles interleaved (independent accumulator chains).
+                    uint32_t a[4][4];
                     if constexpr (BITS == 4) {
                         const int off = (((2 * G + (t >> 1)) ^ g) << 4) + (t & 1) * 8;
-                        const uint2 a = *reinterpret_cast<const uint2 *>(sw + r0 * 128 + off);
-                        const uint2 b = *reinterpret_cast<const uint2 *>(sw + (r0 + 8) * 128 + off);
-                        w0[0] = a.x; w0[1] = a.y; w1[0] = b.x; w1[1] = b.y;
+                        const uint2 u0 = *reinterpret_cast<const uint2 *>(sw + r0 * 128 + off);
+                        const uint2 u1 = *reinterpret_cast<const uint2 *>(sw + (r0 + 8) * 128 + off);
+                        const uint32_t w0[2] = {u0.x, u0.y}, w1[2] = {u1.x, u1.y};
+#pragma unroll
+                        for (int s = 0; s < 4; ++s) {
+                            const int p0 = 2 * (s & 1);
+                            a[s][0] = dec4(w0[s >> 1], p0);
+                            a[s][1] = dec4(w1[s >> 1], p0);
+                            a[s][2] = dec4(w0[s >> 1], p0 + 1);
+                            a[s][3] = dec4(w1[s >> 1], p0 + 1);
+                        }
                     } else {
                         const int off = ((4 * G + t) ^ g) << 4;
-                        const uint4 a = *reinterpret_cast<const uint4 *>(sw + r0 * 128 + off);
-                        const uint4 b = *reinterpret_cast<const uint4 *>(sw + (r0 + 8) * 128 + off);
-                        w0[0] = a.x; w0[1] = a.y; w0[2] = a.z; w0[3] = a.w;
-                        w1[0] = b.x; w1[1] = b.y; w1[2] = b.z; w1[3] = b.w;
+                        const uint4 u0 = *reinterpret_cast<const uint4 *>(sw + r0 * 128 + off);
+                        const uint4 u1 = *reinterpret_cast<const uint4 *>(sw + (r0 + 8) * 128 + off);
+                        const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+                        for (int s = 0; s < 4; ++s) {
+                            a[s][0] = dec8(w0[s], 0);
+                            a[s][1] = dec8(w1[s], 0);
+                            a[s][2] = dec8(w0[s], 2);
+                            a[s][3] = dec8(w1[s], 2);
+                        }
                     }
-                    const uint32_t s_w0 = sv[nt][0][G >> 1], s_w1 = sv[nt][1][G >> 1];
-                    const uint32_t b_w0 = bv[nt][0][G >> 1], b_w1 = bv[nt][1][G >> 1];
+                    float c[MT][4];
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
+#pragma unroll
+                    for (int s = 0; s < 4; ++s)
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            const uint32_t b0 = BITS == 4 ? xf[mt][4 * (s >> 1) + 2 * (s & 1)] : xf[mt][2 * s];
+                            const uint32_t b1 = BITS == 4 ? xf[mt][4 * (s >> 1) + 2 * (s & 1) + 1] : xf[mt][2 * s + 1];
+                            mma_bf16_16816(c[mt], a[s], b0, b1, c[mt]);
+                        }
+                    const uint32_t s_w0 = sv[0][G >> 1], s_w1 = sv[1][G >> 1];
+                    const uint32_t b_w0 = bv[0][G >> 1], b_w1 = bv[1][G >> 1];
                     const float s0 = __uint_as_float((G & 1) ? (s_w0 & 0xFFFF0000u) : (s_w0 << 16));
                     const float s1 = __uint_as_float((G & 1) ? (s_w1 & 0xFFFF0000u) : (s_w1 << 16));
                     float q0 = __uint_as_float((G & 1) ? (b_w0 & 0xFFFF0000u) : (b_w0 << 16));
@@ -525,55 +542,88 @@ __global__ void __launch_bounds__(32 * (CW + 1), 1)
                         q0 = fmaf(-128.0f, s0, q0);
                         q1 = fmaf(-128.0f, s1, q1);
                     }
-                    float c[MT][4];
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        uint32_t a[4], b0[MT], b1[MT];
-                        if constexpr (BITS == 4) {
-                            const int p0 = 2 * (s & 1);
-                            const uint32_t u0 = w0[s >> 1], u1 = w1[s >> 1];
-                            a[0] = dec4(u0, p0);
-                            a[1] = dec4(u1, p0);
-                            a[2] = dec4(u0, p0 + 1);
-                            a[3] = dec4(u1, p0 + 1);
-#pragma unroll
-                            for (int mt = 0; mt < MT; ++mt) {
-                                b0[mt] = xf[mt][4 * (s >> 1) + p0];
-                                b1[mt] = xf[mt][4 * (s >> 1) + p0 + 1];
-                            }
-                        } else {
-                            a[0] = dec8(w0[s], 0);
-                            a[1] = dec8(w1[s], 0);
-                            a[2] = dec8(w0[s], 2);
-                            a[3] = dec8(w1[s], 2);
-#pragma unroll
-                            for (int mt = 0; mt < MT; ++mt) {
-                                b0[mt] = xf[mt][2 * s];
-                                b1[mt] = xf[mt][2 * s + 1];
-                            }
-                        }
-#pragma unroll
-                        for (int mt = 0; mt < MT; ++mt) mma_bf16_16816(c[mt], a, b0[mt], b1[mt], c[mt]);
-                    }
+                    const uint64_t s0p = f2_pack(s0, s0), s1p = f2_pack(s1, s1);
+                    const uint64_t q0p = f2_pack(q0, q0), q1p = f2_pack(q1, q1);
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
-                        acc[nt][mt][0] = fmaf(s0, c[mt][0], fmaf(q0, X[mt].x, acc[nt][mt][0]));
-                        acc[nt][mt][1] = fmaf(s0, c[mt][1], fmaf(q0, X[mt].y, acc[nt][mt][1]));
-                        acc[nt][mt][2] = fmaf(s1, c[mt][2], fmaf(q1, X[mt].x, acc[nt][mt][2]));
-                        acc[nt][mt][3] = fmaf(s1, c[mt][3], fmaf(q1, X[mt].y, acc[nt][mt][3]));
+                        const uint64_t xsum = *reinterpret_cast<const uint64_t *>(xs + G * 16 + 8 * mt + 2 * t);
+                        acc[mt][0] = fma_f32x2(s0p, f2_pack(c[mt][0], c[mt][1]), fma_f32x2(q0p, xsum, acc[mt][0]));
+                        acc[mt][1] = fma_f32x2(s1p, f2_pack(c[mt][2], c[mt][3]), fma_f32x2(q1p, xsum, acc[mt][1]));
                     }
                 }
+                // The stage is refilled by TMA (async proxy) after this release;
+                // order this warp's generic-proxy reads of it first.
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[stage]);
+                if (++stage == S) { stage = 0; phase ^= 1; }
             }
-            // The stage is refilled by TMA (async proxy) after this release;
-            // order this warp's generic-proxy reads of it first.
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[stage]);
-            if (++stage == S) { stage = 0; phase ^= 1; }
+            float accf[MT][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                accf[mt][0] = __uint_as_float(static_cast<uint32_t>(acc[mt][0]));
+                accf[mt][1] = __uint_as_float(static_cast<uint32_t>(acc[mt][0] >> 32));
+                accf[mt][2] = __uint_as_float(static_cast<uint32_t>(acc[mt][1]));
+                accf[mt][3] = __uint_as_float(static_cast<uint32_t>(acc[mt][1] >> 32));
+            }
+            segment_epilogue<MT>(p, accf, blk, warp, g, t, lane, tid, flag);
         }
-        segment_epilogue<MT, NT, CW>(p, acc, split, blk, warp, g, t, lane, tid, flag);
+    }
+}
+
+// Activations into the kernel's layout: dst[m][k] = bf16(src) in pair order
+// (4-bit) or natural order (8-bit).  mode 0: src is bf16 x; mode 1: src is
+// rmsnorm of the f32 residual stream h with the per-16-column sums of squares
+// `ss` ([ss_tiles][16]) and weights gamma.
+__global__ void prep_kernel(const void *src, int64_t ld_src, int mode, const float *ss, int ss_tiles,
+                            const uint16_t *gamma, float eps, int M, int K, int pair_order, uint16_t *dst,
+                            int64_t ld_dst) {
+    __shared__ float rms[16];
+    if (mode == 1) {
+        // 1/rms per row: one warp per row, fixed summation order.
+        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int m = w; m < M; m += blockDim.x / 32) {
+            float sum = 0.0f;
+            for (int tl = lane; tl < ss_tiles; tl += 32) sum += ss[tl * 16 + m];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) rms[m] = rsqrtf(sum / static_cast<float>(K) + eps);
+        }
+        __syncthreads();
+    }
+    const int64_t words = static_cast<int64_t>(M) * (K / 8);
+    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < words;
+         c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int m = static_cast<int>(c / (K / 8));
+        const int k0 = static_cast<int>(c % (K / 8)) * 8;
+        uint32_t v[4];
+        if (mode == 1) {
+            const float4 *hp = reinterpret_cast<const float4 *>(static_cast<const float *>(src) + m * ld_src + k0);
+            const float4 h0 = hp[0], h1 = hp[1];
+            const uint4 gm = *reinterpret_cast<const uint4 *>(gamma + k0);
+            const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            const uint32_t gw[4] = {gm.x, gm.y, gm.z, gm.w};
+            const float r = rms[m];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t lo = f32_to_bf16_bits(hv[2 * e] * r * __uint_as_float(gw[e] << 16));
+                const uint32_t hi = f32_to_bf16_bits(hv[2 * e + 1] * r * __uint_as_float(gw[e] & 0xFFFF0000u));
+                v[e] = lo | (hi << 16);
+            }
+        } else {
+            const uint4 u = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + m * ld_src + k0);
+            v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+        }
+        uint4 o;
+        if (pair_order) {  // [x0 x4 x1 x5 x2 x6 x3 x7]
+            o.x = prmt(v[0], v[2], 0x5410u);
+            o.y = prmt(v[0], v[2], 0x7632u);
+            o.z = prmt(v[1], v[3], 0x5410u);
+            o.w = prmt(v[1], v[3], 0x7632u);
+        } else {
+            o = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+        *reinterpret_cast<uint4 *>(dst + m * ld_dst + k0) = o;
     }
 }
 
@@ -593,92 +643,75 @@ bool qmv_supported(const QmmArgs &a, const char **why) {
     if (!al(a.w.ptr, 16) || (a.w.row_stride * 4) % 16) return no("qmv: packed rows must be 16-byte aligned");
     if (!al(a.s.ptr, 16) || !al(a.b.ptr, 16) || (a.s.row_stride * 2) % 16 || (a.b.row_stride * 2) % 16)
         return no("qmv: parameter rows must be 16-byte aligned");
-    if ((a.N + 255) / 256 > kMaxTiles) return no("qmv: N beyond the arrival-counter region");
+    if ((a.N + qmv::ROWS - 1) / qmv::ROWS > kMaxTiles) return no("qmv: N beyond the arrival-counter region");
     if (a.N >= (int64_t(1) << 31) || a.K >= (int64_t(1) << 30)) return no("qmv: size beyond 32-bit indexing");
     return true;
 }
 
 namespace {
 
-// M <= 8: one column tile, 16 consumer warps of one 16-row tile each
-// (256-row blocks).  M > 8: two column tiles; 8 consumer warps of two 16-row
-// tiles each (256-row blocks) so each activation fragment feeds two tiles.
-struct Variant {
-    int nt, cw, rows, stage_bytes;
-};
-Variant variant_of(const QmmArgs &a) {
-    if (a.M > 8) return {2, 8, qmv::Geom<2, 8>::ROWS, qmv::Geom<2, 8>::STAGE_BYTES};
-    return {1, 16, qmv::Geom<1, 16>::ROWS, qmv::Geom<1, 16>::STAGE_BYTES};
-}
-
-int x_bytes(const QmmArgs &a, int ks) { return static_cast<int>(a.M) * (ks + qmv::XS_PAD) * 2 + (ks / 64) * 16 * 4; }
-
 constexpr int kSmemCap = 227 * 1024;
-constexpr int kMinRing = 2 * 40 * 1024;   // keep >= 80 KB of weights in flight
-constexpr int kMaxRing = 128 * 1024;
+constexpr int kOverhead = 1024 + qmv::MAX_STAGES * 4 * 16 * 4 + 3 * qmv::MAX_STAGES * 8 + 64;
+
+int stage_bytes(int bits) { return bits == 4 ? qmv::Shape<4>::BYTES : qmv::Shape<8>::BYTES; }
 
 }  // namespace
 
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     QmvPlan p{};
-    const Variant v = variant_of(a);
-    const int nk = static_cast<int>(a.K / 512);
-    const int overhead = 1024 + 2 * qmv::MAX_STAGES * 8 + 64 + 20 * 16 * 4;
-    // K splits: the smallest count whose x slice fits next to the ring, raised
-    // towards the count that balances the two on-chip costs of stream-K --
-    // every CTA stages its x slice (grid * M * K/S * 2 bytes) while every
-    // extra split adds partial sums (about 8 * S * M * N bytes) -- which is
-    // minimised near S = sqrt(grid * K / (4 * N)).
-    int smin = 0;
-    for (int s = 1; s <= nk; ++s) {
-        if (nk % s) continue;
-        if (overhead + x_bytes(a, static_cast<int>(a.K / s)) + std::max(kMinRing, 2 * v.stage_bytes) <= kSmemCap) {
-            smin = s;
-            break;
-        }
-    }
-    if (smin == 0) return p;
-    const double s_opt = std::sqrt(static_cast<double>(num_sms) * a.K / (4.0 * a.N));
-    int splits = smin;
-    for (int s = smin; s <= nk; ++s)
-        if (nk % s == 0 && s <= s_opt * 1.5) splits = s;
-    const int ks = static_cast<int>(a.K / splits);
-    const int ring_room = kSmemCap - overhead - x_bytes(a, ks);
-    const int stages = std::min(qmv::MAX_STAGES, std::min(ring_room, kMaxRing) / v.stage_bytes);
+    const int sb = stage_bytes(a.bits);
+    const int stages = std::min(qmv::MAX_STAGES, (kSmemCap - kOverhead) / sb);
     if (stages < 2) return p;
-    const int64_t nblocks = (a.N + v.rows - 1) / v.rows;
+    const int64_t nblocks = (a.N + qmv::ROWS - 1) / qmv::ROWS;
     const int kps = a.bits == 4 ? 256 : 128;
-    const int64_t spb = ks / kps;
-    const int64_t items = nblocks * spb * splits;
+    const int64_t spb = a.K / kps;
+    const int64_t items = nblocks * spb;
     const int grid = static_cast<int>(std::min<int64_t>(num_sms, items));
-    // Upper bound of contributors per block: per split, a block spans at most
-    // ceil(spb / floor(items/grid)) + 1 CTAs.
+    // Contributors per block: a block spans at most ceil(spb / floor(items/grid)) + 1 CTAs.
     const int64_t per_cta = std::max<int64_t>(1, items / grid);
-    const int max_slots = static_cast<int>(splits * ((spb + per_cta - 1) / per_cta + 1));
-    const size_t need = kPartialOffset + static_cast<size_t>(nblocks) * max_slots * a.M * v.rows * 4;
+    const int max_slots = static_cast<int>(std::min<int64_t>((spb + per_cta - 1) / per_cta + 1, grid));
+    const size_t need = kPartialOffset + static_cast<size_t>(nblocks) * max_slots * a.M * qmv::ROWS * 4 +
+                        qmv_prep_bytes(a);
     if (need > workspace_bytes) return p;
-    p.splits = splits;
-    p.ks = ks;
+    p.splits = 1;
+    p.ks = static_cast<int>(a.K);
     p.grid_n = grid;
     p.stages = stages;
     p.max_slots = max_slots;
-    p.smem_bytes = overhead + x_bytes(a, ks) + stages * v.stage_bytes;
+    p.smem_bytes = kOverhead + stages * sb;
     return p;
 }
 
-size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p) {
-    const Variant v = variant_of(a);
-    const int64_t nblocks = (a.N + v.rows - 1) / v.rows;
-    return kPartialOffset + static_cast<size_t>(nblocks) * p.max_slots * a.M * v.rows * 4;
+size_t qmv_prep_bytes(const QmmArgs &a) {
+    // 4-bit codes read x in pair order: a converted copy lives at the end of
+    // the workspace (aligned to 1 KiB).
+    return a.bits == 4 ? ((static_cast<size_t>(a.M) * a.K * 2 + 1023) / 1024) * 1024 : 0;
 }
 
-template <int BITS, int MT, int NT, int CW>
+size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p) {
+    const int64_t nblocks = (a.N + qmv::ROWS - 1) / qmv::ROWS;
+    return kPartialOffset + static_cast<size_t>(nblocks) * p.max_slots * a.M * qmv::ROWS * 4 + qmv_prep_bytes(a);
+}
+
+template <int BITS, int MT>
 static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, const CUtensorMap &bm,
-                              const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream) {
-    auto kern = qmv::qmv_kernel<BITS, MT, NT, CW>;
+                              const CUtensorMap &xm, const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream) {
+    auto kern = qmv::qmv_kernel<BITS, MT>;
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(kern), plan.smem_bytes);
     if (e != cudaSuccess) return e;
-    kern<<<plan.grid_n, 32 * (CW + 1), plan.smem_bytes, stream>>>(wm, sm, bm, p);
+    kern<<<plan.grid_n, qmv::THREADS, plan.smem_bytes, stream>>>(wm, sm, bm, xm, p);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qmv_prep(const void *src, int64_t ld_src, int mode, const float *ss, int ss_tiles,
+                            const uint16_t *gamma, float eps, int M, int K, int bits, uint16_t *dst, int64_t ld_dst,
+                            cudaStream_t stream) {
+    const int64_t words = static_cast<int64_t>(M) * (K / 8);
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::min<int64_t>((words + threads - 1) / threads, 1184));
+    qmv::prep_kernel<<<blocks, threads, 0, stream>>>(src, ld_src, mode, ss, ss_tiles, gamma, eps, M, K, bits == 4 ? 1 : 0,
+                                                     dst, ld_dst);
     count_launch();
     return cudaGetLastError();
 }
@@ -686,20 +719,15 @@ static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, cons
 cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, cudaStream_t stream,
                        const QmvFusion *fusion) {
     if (plan.splits < 1) return cudaErrorInvalidValue;
-    const Variant v = variant_of(a);
     qmv::Params p{};
-    p.x = static_cast<const uint16_t *>(a.x.ptr);
-    p.ldx = a.x.row_stride;
     p.y = a.y;
     p.ldy = a.ldy;
     p.M = static_cast<int>(a.M);
     p.N = static_cast<int>(a.N);
     p.K = static_cast<int>(a.K);
-    p.splits = plan.splits;
-    p.ks = plan.ks;
-    p.nblocks = static_cast<int>((a.N + v.rows - 1) / v.rows);
-    p.spb = plan.ks / (a.bits == 4 ? 256 : 128);
-    p.items = static_cast<int64_t>(p.nblocks) * p.spb * p.splits;
+    p.nblocks = static_cast<int>((a.N + qmv::ROWS - 1) / qmv::ROWS);
+    p.spb = static_cast<int>(a.K / (a.bits == 4 ? 256 : 128));
+    p.items = static_cast<int64_t>(p.nblocks) * p.spb;
     p.stages = plan.stages;
     p.max_slots = plan.max_slots;
     p.y_bf16 = a.y_bf16;
@@ -708,20 +736,35 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     p.status = reinterpret_cast<unsigned *>(ws);
     p.counters = reinterpret_cast<unsigned *>(ws + kCounterOffset);
     p.partial = reinterpret_cast<float *>(ws + kPartialOffset);
-    const CUtensorMap *wm, *sm, *bm;
+    // Activations: already in the kernel's order (x_mode 1), or converted
+    // into the workspace tail here (4-bit codes need pair order).
+    const void *xq = a.x.ptr;
+    int64_t ldxq = a.x.row_stride;
+    const bool in_order = fusion && fusion->x_mode == 1;
+    if (a.bits == 4 && !in_order) {
+        uint16_t *dst = reinterpret_cast<uint16_t *>(ws + qmv_workspace_bytes(a, plan) - qmv_prep_bytes(a));
+        cudaError_t e = launch_qmv_prep(a.x.ptr, a.x.row_stride, 0, nullptr, 0, nullptr, 0.f, p.M, p.K, 4, dst, p.K,
+                                        stream);
+        if (e != cudaSuccess) return e;
+        xq = dst;
+        ldxq = p.K;
+    }
+    const CUtensorMap *wm, *sm, *bm, *xm;
     const uint64_t words = static_cast<uint64_t>(a.K) * a.bits / 32;
-    if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32, v.rows,
-                                    CU_TENSOR_MAP_SWIZZLE_128B)) ||
+    if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32,
+                                    qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_128B)) ||
         !(sm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2, 8,
-                                    v.rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+                                    qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
         !(bm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2, 8,
-                                    v.rows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+                                    qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+        !(xm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xq, a.K, a.M, ldxq * 2, 64, 16,
+                                    CU_TENSOR_MAP_SWIZZLE_128B)))
         return cudaErrorInvalidValue;
     if (a.M > 8)
-        return a.bits == 4 ? launch_cfg<4, 2, 2, 8>(*wm, *sm, *bm, p, plan, stream)
-                           : launch_cfg<8, 2, 2, 8>(*wm, *sm, *bm, p, plan, stream);
-    return a.bits == 4 ? launch_cfg<4, 1, 1, 16>(*wm, *sm, *bm, p, plan, stream)
-                       : launch_cfg<8, 1, 1, 16>(*wm, *sm, *bm, p, plan, stream);
+        return a.bits == 4 ? launch_cfg<4, 2>(*wm, *sm, *bm, *xm, p, plan, stream)
+                           : launch_cfg<8, 2>(*wm, *sm, *bm, *xm, p, plan, stream);
+    return a.bits == 4 ? launch_cfg<4, 1>(*wm, *sm, *bm, *xm, p, plan, stream)
+                       : launch_cfg<8, 1>(*wm, *sm, *bm, *xm, p, plan, stream);
 }
 
 }  // namespace afb

@@ -68,6 +68,18 @@ AFB_DEVICE bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, u
     }
 }
 
+// Bounded wait that ignores the abort flag: used on the way out of a kernel
+// to let copies already in flight land before shared memory is released.
+// Returns false after `limit_ns`.
+AFB_DEVICE bool mbar_wait_drain(uint64_t *bar, uint32_t parity, uint64_t limit_ns = 1000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && globaltimer() - start > limit_ns) return false;
+    }
+}
+
 // 2D tiled TMA load global -> shared, completion counted on `bar`.
 AFB_DEVICE void tma_load_2d(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1) {
     asm volatile(

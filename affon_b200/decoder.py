@@ -3,7 +3,10 @@
 Every projection is a 4-bit (or 8-bit) affine group-quantized linear
 (`quantized_matmul` layout: codes packed little-endian into u32 along K,
 group 64, bf16 scale and bias), run by the decode qmv with the decoder's
-RMSNorm, residual adds, SiLU-gated product and final argmax fused in.
+residual adds, SiLU-gated product and final argmax fused into its epilogue.
+RMSNorm is one small kernel that also writes the normalized activations in
+the qmv's column order; attention and the SiLU epilogue write theirs in that
+order directly.
 Attention is the affon_b200 decode-attention kernel (RoPE and KV-cache
 append fused).  The reference has no quantized decoder; the layer structure
 follows its Llama program (packages/@affon/models/src/llama/model.ts:64-78:
@@ -143,6 +146,7 @@ class QuantizedDecoder:
         self.history = torch.zeros((max_steps, batch), dtype=torch.int32, device=dev)
         self.h = torch.zeros((batch, c.d_model), dtype=torch.float32, device=dev)
         self.ss = torch.zeros((c.d_model // 16, 16), dtype=torch.float32, device=dev)
+        self.xq = torch.zeros((batch, c.d_model), dtype=torch.bfloat16, device=dev)   # normalized x, qmv order
         self.qkv = torch.zeros((batch, c.qkv_rows), dtype=torch.bfloat16, device=dev)
         self.attn = torch.zeros((batch, c.q_heads * c.head_dim), dtype=torch.bfloat16, device=dev)
         self.act = torch.zeros((batch, c.ffn), dtype=torch.bfloat16, device=dev)
@@ -165,27 +169,30 @@ class QuantizedDecoder:
                                        1.0 / math.sqrt(hd), 0, c.q_heads * hd, (c.q_heads + c.kv_heads) * hd, 0,
                                        c.qkv_rows, c.q_heads * hd)
         ptr = lambda t: ctypes.c_void_p(t.data_ptr())
-        fz = lambda **kw: _lib.QmvFusion(struct_size=ctypes.sizeof(_lib.QmvFusion), eps=c.eps, **kw)
-        norm = lambda g: dict(x_mode=1, h_in=ptr(self.h), ld_h_in=c.d_model, ss_in=ptr(self.ss),
-                              ss_tiles=c.d_model // 16, gamma=ptr(g))
+        pair = 1 if c.bits == 4 else 0          # producers write the 4-bit qmv's pair order
+        self.attn_desc.out_pair_order = pair
+        fz = lambda **kw: _lib.QmvFusion(struct_size=ctypes.sizeof(_lib.QmvFusion), x_mode=1, **kw)
         resid = dict(epilogue=_lib.EPI_RESID, h_out=ptr(self.h), ld_h_out=c.d_model, ss_out=ptr(self.ss))
+        xq = ptr(self.xq)
         self.calls = []
-        layer_bytes = c.d_model * hd * c.kv_heads * self.cap * 2  # not used; keeps shapes visible
-        del layer_bytes
         for i, lay in enumerate(self.layers):
             q, o, gu, dn = lay["qkv"], lay["o"], lay["gate_up"], lay["down"]
-            self.calls.append(("qmv", q.desc(B), None, q, ptr(self.qkv),
-                               fz(**norm(lay["attn_norm"]), epilogue=_lib.EPI_STORE)))
+            self.calls.append(("norm", lay["attn_norm"]))
+            self.calls.append(("qmv", q.desc(B), xq, q, ptr(self.qkv), fz(epilogue=_lib.EPI_STORE)))
             self.calls.append(("attn", i))
             self.calls.append(("qmv", o.desc(B), ptr(self.attn), o, None, fz(**resid)))
-            self.calls.append(("qmv", gu.desc(B), None, gu, None,
-                               fz(**norm(lay["ffn_norm"]), epilogue=_lib.EPI_SILU_MUL, act=ptr(self.act),
-                                  ld_act=c.ffn)))
+            self.calls.append(("norm", lay["ffn_norm"]))
+            self.calls.append(("qmv", gu.desc(B), xq, gu, None,
+                               fz(epilogue=_lib.EPI_SILU_MUL, act=ptr(self.act), ld_act=c.ffn, act_pair_order=pair)))
             self.calls.append(("qmv", dn.desc(B), ptr(self.act), dn, None, fz(**resid)))
         lm = self.lm_head
-        self.calls.append(("qmv", lm.desc(B), None, lm, None,
-                           fz(**norm(self.final_norm), epilogue=_lib.EPI_ARGMAX, amax=ptr(self.amax))))
+        self.calls.append(("norm", self.final_norm))
+        self.calls.append(("qmv", lm.desc(B), xq, lm, None, fz(epilogue=_lib.EPI_ARGMAX, amax=ptr(self.amax))))
         self._kv_layer = [(self.k_cache[i], self.v_cache[i]) for i in range(c.layers)]
+
+    def launches_per_step(self):
+        """Kernels one decode step launches: embed, then one per call, then finalize."""
+        return 2 + len(self.calls)
 
     def _launch_step(self, finalize=True):
         L, ctx = self._L, self.ctx
@@ -193,7 +200,11 @@ class QuantizedDecoder:
         check(L.affon_b200_embed(ctx, self.embed.data_ptr(), c.d_model, self.tokens.data_ptr(), self.B, c.d_model,
                                  self.h.data_ptr(), self.ss.data_ptr(), self.amax.data_ptr()), "embed")
         for call in self.calls:
-            if call[0] == "attn":
+            if call[0] == "norm":
+                check(L.affon_b200_qmv_prep(ctx, 1, self.h.data_ptr(), c.d_model, self.ss.data_ptr(), c.d_model // 16,
+                                            call[1].data_ptr(), ctypes.c_float(c.eps), self.B, c.d_model, c.bits,
+                                            self.xq.data_ptr(), c.d_model), "qmv_prep")
+            elif call[0] == "attn":
                 kc, vc = self._kv_layer[call[1]]
                 check(L.affon_b200_decode_attention(ctx, ctypes.byref(self.attn_desc), self.qkv.data_ptr(),
                                                     kc.data_ptr(), vc.data_ptr(), self.cos.data_ptr(),

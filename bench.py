@@ -305,8 +305,9 @@ def run_decode(args, rank, world, dev):
         torch.cuda.synchronize(dev)
     ms = ev0.elapsed_time(ev1) / args.steps
     # graph replays do not pass through the C ABI, so count the launches of one
-    # captured step (embed + per layer 4 qmv + attention, LM head, finalize)
-    launches = args.steps * (2 + 5 * cfg.layers + 1)
+    # captured step (embed; per layer 2 norms, 4 qmv, attention; final norm,
+    # LM head; finalize)
+    launches = args.steps * dec.launches_per_step()
     ms_max = ms
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -340,8 +341,8 @@ def run_decode(args, rank, world, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    # dominant kernel, timed live: the gate/up qmv of layer 0 (largest share of
-    # the weight bytes), with its fused rmsnorm prologue and silu*mul epilogue
+    # dominant kernel, timed live: the gate/up qmv (largest share of the weight
+    # bytes) with its silu*mul epilogue, reading the normalized activations
     lay = dec.layers[0]
     gu = lay["gate_up"]
     desc = gu.desc(B)
@@ -349,10 +350,6 @@ def run_decode(args, rank, world, dev):
     for call in dec.calls:
         if call[0] == "qmv" and call[3] is gu:
             fus = call[5]
-    def gu_launch(s):
-        check(L.affon_b200_ctx_set_stream(dec.ctx, s.cuda_stream))
-        check(L.affon_b200_qmv_fused(dec.ctx, ctypes.byref(desc), None, gu.w.data_ptr(), gu.s.data_ptr(),
-                                     gu.b.data_ptr(), None, ctypes.byref(fus)))
     # rotate over all 32 layers' gate/up weights so launches stream from HBM
     gus = [l["gate_up"] for l in dec.layers]
     idx = [0]
@@ -360,11 +357,11 @@ def run_decode(args, rank, world, dev):
         lin = gus[idx[0] % len(gus)]
         idx[0] += 1
         check(L.affon_b200_ctx_set_stream(dec.ctx, s.cuda_stream))
-        check(L.affon_b200_qmv_fused(dec.ctx, ctypes.byref(desc), None, lin.w.data_ptr(), lin.s.data_ptr(),
-                                     lin.b.data_ptr(), None, ctypes.byref(fus)))
+        check(L.affon_b200_qmv_fused(dec.ctx, ctypes.byref(desc), dec.xq.data_ptr(), lin.w.data_ptr(),
+                                     lin.s.data_ptr(), lin.b.data_ptr(), None, ctypes.byref(fus)))
     gu_ms = _graph_time_ms(gu_launch_rot, 64, dev)
     dec.set_stream(torch.cuda.current_stream(dev))
-    gu_bytes = gu.N * gu.K * gu.bits // 8 + gu.N * (gu.K // 64) * 4 + B * gu.K * 4 + B * (gu.N // 2) * 2
+    gu_bytes = gu.N * gu.K * gu.bits // 8 + gu.N * (gu.K // 64) * 4 + B * gu.K * 2 + B * (gu.N // 2) * 2
     dec.close()
 
     pk, pk_kind = peaks()
@@ -392,7 +389,7 @@ def run_decode(args, rank, world, dev):
         "e2e": {"value": round(B * world / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 4,
                 "d2h_bytes_per_step": B * 4, "ms_per_step": round(e2e_ms, 4),
                 "path": "decoder graph replay with pinned token H2D/D2H and host read each step"},
-        "roofline": {"bound": "hbm", "kernel": "qmv gate/up (rmsnorm prologue, silu*mul epilogue), M=16 N=28672 K=4096",
+        "roofline": {"bound": "hbm", "kernel": "qmv gate/up (silu*mul epilogue), M=16 N=28672 K=4096",
                      "achieved": round(gu_achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gu_achieved / pk["hbm_gbs"], 4), "traffic": traffic,
                      "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json)" if pk_kind == "measured" else

@@ -99,7 +99,7 @@ typedef struct affon_b200_selection {
     char implementation_id[64]; /* e.g. "cuda_quantized_matmul.sm100_qmv_b4_g64" */
     int32_t implementation_version;
     int32_t numerical_class;    /* affon_b200_numerics */
-    int32_t splits;             /* split-K factor the launch will use (1 = none) */
+    int32_t splits;             /* K segments combined per output tile, at most (1 = none) */
     int32_t reserved;
     char reason[256];
 } affon_b200_selection;
@@ -189,26 +189,32 @@ int affon_b200_qmv_noalloc(const affon_b200_qmm_desc *desc, const void *x, const
  * quantized linears, with the decoder's norms, residual adds, gated
  * activation and argmax fused into the qmv. */
 
-/* Fusions of the decode qmv.  x_mode 1: the activations are
- * bf16(h_in[m][k] * rsqrt(sum_k h_in[m][k]^2 / K + eps) * gamma[k]), the sum
- * taken from ss_in ([ss_tiles][16] f32 partial sums, any order of tiles,
- * summed in a fixed order).  epilogue 1: h_out[m][n] += y[m][n] (f32) and
- * ss_out[n/16][m] = sum of the squares of the 16 updated h_out entries;
- * epilogue 2: act[m][8*(n/16) + n%8] = bf16(silu(y[m][n]) * y[m][n+8]) for
- * n%16 < 8 (weight tiles of 8 gate rows then the 8 matching up rows);
- * epilogue 3: atomicMax(amax[m], key(y[m][n]) << 32 | (0xffffffff - n)) with an
- * order-preserving key (lowest index wins ties; amax must start at 0). */
+/* Activations in the decode qmv's order.  For 4-bit codes the decode qmv
+ * reads x in "pair order": within every 8 consecutive columns,
+ * [x0 x4 x1 x5 x2 x6 x3 x7] (8-bit codes: natural order).  mode 0: src is
+ * bf16 [rows][ld_src]; mode 1: src is an f32 residual stream h and the output
+ * is bf16(h[m][k] * rsqrt(sum_k h[m][k]^2 / cols + eps) * gamma[k]), the sum
+ * taken from ss ([ss_tiles][16] f32 partial sums, summed in a fixed order).
+ * rows <= 16; dst is bf16 [rows][ld_dst]. */
+int affon_b200_qmv_prep(affon_b200_ctx *ctx, int mode, const void *src, int64_t ld_src, const float *ss,
+                        int ss_tiles, const void *gamma, float eps, int rows, int cols, int bits, void *dst,
+                        int64_t ld_dst);
+
+/* Fusions of the decode qmv.  x_mode 0: x is natural-order bf16 (the call
+ * converts it); x_mode 1: x is already in the qmv's order (affon_b200_qmv_prep
+ * or a fused producer wrote it).  epilogue 0: store y; epilogue 1:
+ * h_out[m][n] += y[m][n] (f32) and ss_out[n/16][m] = sum of the squares of the
+ * 16 updated h_out entries; epilogue 2: for n%16 < 8 (weight tiles of 8 gate
+ * rows then the 8 matching up rows), act[m][8*(n/16) + n%8] =
+ * bf16(silu(y[m][n]) * y[m][n+8]), in pair order within each 8 columns when
+ * act_pair_order is set; epilogue 3: atomicMax(amax[m], key(y[m][n]) << 32 |
+ * (0xffffffff - n)) with an order-preserving key (lowest index wins ties;
+ * amax must start at 0). */
 typedef struct affon_b200_qmv_fusion {
     uint32_t struct_size;
     int32_t x_mode;
-    const float *h_in;
-    int64_t ld_h_in;
-    const float *ss_in;
-    int32_t ss_tiles;
-    float eps;
-    const void *gamma;
     int32_t epilogue;
-    int32_t reserved;
+    int32_t act_pair_order;
     float *h_out;
     int64_t ld_h_out;
     float *ss_out;
@@ -230,7 +236,7 @@ typedef struct affon_b200_attn_desc {
     int32_t batch, q_heads, kv_heads, head_dim, capacity;
     float scale;
     int32_t q_offset, k_offset, v_offset;
-    int32_t reserved;
+    int32_t out_pair_order; /* write the output in 4-bit qmv pair order */
     int64_t ld_qkv, ld_out;
 } affon_b200_attn_desc;
 

@@ -140,3 +140,45 @@ def test_graph_replay_equals_eager_steps(dec):
     assert torch.equal(dec.history[:3], eager_hist)
     assert torch.equal(dec.h, eager_h)
     assert int(dec.pos.item()) == 19
+
+
+def _pair_order(x):
+    """4-bit qmv column order: within each 8 columns [x0 x4 x1 x5 x2 x6 x3 x7]."""
+    r, k = x.shape
+    return x.reshape(r, k // 8, 2, 4).transpose(-1, -2).reshape(r, k)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_qmv_prep_orders_and_normalizes(bits):
+    import ctypes
+    from affon_b200 import _lib
+    from affon_b200.core import check
+    dev = torch.device("cuda", 0)
+    L = _lib.lib()
+    ctx = ctypes.c_void_p()
+    check(L.affon_b200_ctx_create(0, None, ctypes.byref(ctx)))
+    try:
+        check(L.affon_b200_ctx_set_stream(ctx, torch.cuda.current_stream().cuda_stream))
+        gen = torch.Generator(device=dev).manual_seed(3)
+        M, K = 13, 1024
+        x = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
+        out = torch.zeros((M, K), dtype=torch.bfloat16, device=dev)
+        check(L.affon_b200_qmv_prep(ctx, 0, x.data_ptr(), K, None, 0, None, ctypes.c_float(0.0), M, K, bits,
+                                    out.data_ptr(), K))
+        want = _pair_order(x) if bits == 4 else x
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+        # rmsnorm from an f32 residual stream and its [K/16][16] partial sums of squares
+        h = torch.randn((M, K), generator=gen, device=dev) * 3
+        ss = torch.zeros((K // 16, 16), device=dev)
+        ss[:, :M] = (h * h).reshape(M, K // 16, 16).sum(-1).T
+        g = (1 + 0.1 * torch.randn((K,), generator=gen, device=dev)).to(torch.bfloat16)
+        check(L.affon_b200_qmv_prep(ctx, 1, h.data_ptr(), K, ss.data_ptr(), K // 16, g.data_ptr(),
+                                    ctypes.c_float(1e-5), M, K, bits, out.data_ptr(), K))
+        torch.cuda.synchronize()
+        ref = rms_norm(h, g, 1e-5)
+        ref = _pair_order(ref) if bits == 4 else ref
+        assert float((out.float() - ref).abs().max()) <= 1e-2 * float(ref.abs().max())
+        assert L.affon_b200_ctx_synchronize(ctx) == 0
+    finally:
+        L.affon_b200_ctx_destroy(ctx)
