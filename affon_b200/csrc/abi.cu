@@ -359,8 +359,9 @@ int affon_b200_ctx_synchronize(affon_b200_ctx *ctx) {
     if ((e = cudaMemcpy(&status, ctx->workspace, sizeof status, cudaMemcpyDeviceToHost)) != cudaSuccess)
         return cuda_fail(e, "status read");
     if (status != 0) {
-        const unsigned zero = 0;
-        cudaMemcpy(ctx->workspace, &zero, sizeof zero, cudaMemcpyHostToDevice);
+        // A kernel that gave up may have left arrival counters behind: clear
+        // the status word and the whole counter region for the next launch.
+        cudaMemset(ctx->workspace, 0, afb::kPartialOffset);
         return fail(AFFON_B200_TIMEOUT, "a kernel gave up a bounded wait (device status %u)", status);
     }
     return AFFON_B200_OK;

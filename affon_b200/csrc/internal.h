@@ -38,7 +38,8 @@ struct QmvPlan {
 
 // Context workspace layout: [0, 256) device status words (a bounded wait that
 // gives up writes there); [kCounterOffset, kPartialOffset) split-K arrival
-// counters, zero between launches; [kPartialOffset, ...) f32 partial sums.
+// counters (first half) and completion counters (second half), zero between
+// launches; [kPartialOffset, ...) f32 partial sums.
 constexpr size_t kCounterOffset = 256;
 constexpr int64_t kMaxTiles = 262144;
 constexpr size_t kPartialOffset = kCounterOffset + size_t(kMaxTiles) * 4;

@@ -76,9 +76,11 @@ extern "C" int affon_b200_qmv_noalloc(const affon_b200_qmm_desc *desc, const voi
     if ((rc = scratch_address(device, &scratch))) return rc;
     cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
     // The array keeps the previous call's contents: clear the status word and
-    // the arrival counters this launch can touch before it runs.
+    // the arrival and completion counters this launch can touch before it runs.
     const size_t counters = (static_cast<size_t>(a.N) + 127) / 128 * sizeof(unsigned);
-    if ((e = cudaMemsetAsync(scratch, 0, afb::kCounterOffset + counters, stream)) != cudaSuccess)
+    if ((e = cudaMemsetAsync(scratch, 0, afb::kCounterOffset + counters, stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(static_cast<char *>(scratch) + afb::kCounterOffset + afb::kMaxTiles / 2 * sizeof(unsigned),
+                             0, counters, stream)) != cudaSuccess)
         return afb::set_cuda_error(e, "cudaMemsetAsync(qmv scratch)");
     if ((e = afb::launch_qmv(a, plan, scratch, stream)) != cudaSuccess) return afb::set_cuda_error(e, "qmv launch");
     return AFFON_B200_OK;

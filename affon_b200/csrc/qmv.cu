@@ -4,13 +4,14 @@
 // docs/core/quantized-inference.md:45-67).
 //
 // Streaming.  Persistent CTAs, one per SM.  One producer warp moves each
-// 256-row x 128-byte stage of the packed weight matrix through a ring of
+// 384-row x 128-byte stage of the packed weight matrix through a ring of
 // shared-memory stages with 2D TMA loads (128-byte swizzle), together with the
-// matching 256 x 8 boxes of bf16 scales and biases and the stage's activation
+// matching 384 x 8 boxes of bf16 scales and biases and the stage's activation
 // columns (16 rows x 64 columns per group, 128-byte swizzle).  The ring holds
 // ~190 KB per SM in flight without costing registers, and the activations
-// need no separate staging pass.  Sixteen consumer warps (one 16-row weight
-// tile each) decode the packed words in registers and feed tensor cores.
+// need no separate staging pass.  Twelve consumer warps (two 16-row weight
+// tiles each, so each activation fragment feeds two tiles) decode the packed
+// words in registers and feed tensor cores.
 //
 // Why mma.sync tensor cores at M <= 16: at ~6.5 TB/s a 4-bit weight stream
 // delivers ~13e12 weights/s; decoding each weight to a float and multiplying
@@ -20,8 +21,6 @@
 // tcgen05 MMAs do not fit this shape: each instruction occupies the SM's
 // tensor core for ~146 cycles whatever its N (16..256), so at N <= 16 the
 // 128 x 16 weights per instruction cap a CTA near 7 bytes of codes per cycle.
-// Shifts of the nibble decoder are issued as mul.hi so they run on the FMA
-// pipe beside the logic ops on the ALU pipe.
 //
 // Exact codes, per-group affine in f32: the MMA multiplies the integer codes
 // (4-bit: as 128+q, exact in bf16) by x, giving C_g = sum_{k in g} x*code in
@@ -40,14 +39,17 @@
 // launch_qmv_prep writes that order from natural bf16 x (and, for the decoder,
 // the RMS-normalised residual stream); 8-bit codes use natural order.
 //
-// Work partition (stream-K).  The work is a flat list of items (256-row
+// Work partition (stream-K).  The work is a flat list of items (384-row
 // block, 128-byte K stage).  CTA c takes the items [c*T/C, (c+1)*T/C), so
-// every CTA streams the same number of bytes.  A block that lies inside one
-// CTA is stored directly; a block shared by several CTAs is combined through
-// f32 partials: each contributing CTA writes its slot, and the CTA arriving
-// last (per-block counter) sums the slots in a fixed order and stores y, so
-// results do not depend on scheduling.  That CTA resets the counter for the
-// next launch.
+// every CTA streams the same number of bytes (the grid is the fewest CTAs
+// with the makespan of one CTA per SM).  A block that lies inside one CTA is
+// stored directly; a block shared by several CTAs is combined through f32
+// partials: each contributing CTA writes its slot and counts its arrival on
+// the block's counter.  The launch is cooperative (all CTAs resident), so at
+// the end every contributor waits (bounded) for the block's count, then sums
+// the slots in slot order for its own share of the block's rows and applies
+// the epilogue; results do not depend on scheduling.  The last CTA to finish
+// a block resets its counters for the next launch.
 #include <algorithm>
 #include <cmath>
 
@@ -61,9 +63,11 @@ namespace qmv {
 constexpr int GROUP = 64;
 constexpr int MAX_STAGES = 8;
 constexpr int X_BOX_BYTES = 16 * 128;  // one group of activation columns: 16 rows x 64 bf16
-constexpr int CONSUMERS = 16;          // consumer warps: one 16-row weight tile each, 256-row blocks
-constexpr int NT = 1;                  // 16-row weight tiles per consumer warp
+constexpr int CONSUMERS = 12;          // consumer warps: two 16-row weight tiles each, 384-row blocks
+constexpr int NT = 2;                  // 16-row weight tiles per consumer warp
 constexpr int ROWS = 16 * NT * CONSUMERS;
+constexpr int BOX_ROWS = 128;          // TMA box height for weights, scales and biases
+static_assert(ROWS % BOX_ROWS == 0, "block rows");
 constexpr int THREADS = 32 * (CONSUMERS + 2);  // consumers, producer, sum warp
 
 template <int BITS>
@@ -91,14 +95,10 @@ struct Params {
     QmvFusion f;
 };
 
-__device__ __forceinline__ uint32_t shr_fma_pipe(uint32_t w, int s) {
-    uint32_t r;
-    asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(1u << (32 - s)));
-    return r;
-}
-// Codes p and p+4 of a 4-bit word as the exact bf16 pair (128+q_p, 128+q_{p+4}).
+// Codes p and p+4 of a 4-bit word as the exact bf16 pair (128+q_p, 128+q_{p+4}):
+// one shift and one logic op.
 __device__ __forceinline__ uint32_t dec4(uint32_t w, int p) {
-    return lop3_and_or(p ? shr_fma_pipe(w, 4 * p) : w, 0x000F000Fu, 0x43004300u);
+    return lop3_and_or(p ? (w >> (4 * p)) : w, 0x000F000Fu, 0x43004300u);
 }
 // Bytes i and i+1 of an 8-bit word as an exact bf16 pair (via 2^23 + q in f32).
 __device__ __forceinline__ uint32_t dec8(uint32_t w, int i) {
@@ -219,8 +219,8 @@ __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT
 // Final value v of weight row n for activation row m, one thread per row,
 // 32 consecutive rows per warp (a 16-row tile is one half warp; rows n and
 // n+8 sit in lanes l and l+8).  Called by all 32 lanes with the same m.
-__device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, float v, int lane) {
-    const bool ok = n < p.N;
+__device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, float v, int lane, bool active) {
+    const bool ok = active && n < p.N;
     switch (p.f.epi) {
     case EPI_RESID: {
         float hv = 0.0f;
@@ -239,7 +239,7 @@ __device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, fl
     }
     case EPI_SILU_MUL: {
         const float up = __shfl_down_sync(0xffffffffu, v, 8);
-        if ((lane & 8) == 0 && n + 8 < p.N) {
+        if (active && (lane & 8) == 0 && n + 8 < p.N) {
             const int e = static_cast<int>(n & 7);
             const float silu = v / (1.0f + __expf(-v));
             p.f.act[m * p.f.ld_act + (n >> 4) * 8 + (p.f.act_pair_order ? pair_slot(e) : e)] =
@@ -263,78 +263,115 @@ __device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, fl
     }
 }
 
-// Epilogue of one block segment of this CTA, called by all consumer warps
-// together.  `flag` is a shared-memory word.
-template <int MT>
-__device__ __forceinline__ void segment_epilogue(const Params &p, const float (&acc)[MT][4], int blk, int warp,
-                                                 int g, int t, int lane, int tid, volatile int *flag) {
-    constexpr int CT = CONSUMERS * 32;  // consumer threads
+// Contributors of block blk: CTAs first..first+total-1 (stream-K ranges).
+__device__ __forceinline__ void block_contributors(const Params &p, int blk, int &first, int &total) {
     const int64_t b0 = static_cast<int64_t>(blk) * p.spb;
-    const int first = owner_of(b0, p.items, gridDim.x), last_owner = owner_of(b0 + p.spb - 1, p.items, gridDim.x);
-    const int total = last_owner - first + 1;
+    first = owner_of(b0, p.items, gridDim.x);
+    total = owner_of(b0 + p.spb - 1, p.items, gridDim.x) - first + 1;
+}
+
+// End of one block segment of this CTA, called by all consumer warps
+// together.  A block inside one CTA is finished here.  Otherwise the CTA
+// writes its f32 partial slot and announces it on the block's arrival
+// counter; the sums are formed in combine_blocks once every contributor has
+// written its slot.
+template <int MT>
+__device__ __forceinline__ void segment_epilogue(const Params &p, const float (&acc)[NT][MT][4], int blk, int warp,
+                                                 int g, int t, int tid) {
+    constexpr int CT = CONSUMERS * 32;  // consumer threads
+    int first, total;
+    block_contributors(p, blk, first, total);
     const int64_t nb0 = static_cast<int64_t>(blk) * ROWS;
     if (total == 1) {
-        finish_tile<MT>(p, acc, nb0 + warp * 16, g, t);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) finish_tile<MT>(p, acc[nt], nb0 + (warp * NT + nt) * 16, g, t);
         return;
     }
     const int slot = static_cast<int>(blockIdx.x) - first;
     // partial[((blk * max_slots + slot) * M + m) * ROWS + row]
     float *base = p.partial + static_cast<int64_t>(blk) * p.max_slots * p.M * ROWS;
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int m = 2 * t + 8 * mt + (i & 1);
-            const int r = warp * 16 + g + 8 * (i >> 1);
-            if (m < p.M) base[(static_cast<int64_t>(slot) * p.M + m) * ROWS + r] = acc[mt][i];
-        }
-    // Message passing through the per-block counter (one arrival per
-    // contributing CTA): every thread releases its partials with a gpu-scope
-    // acq_rel fence, the consumer warps meet, one thread takes the ticket,
-    // and in the last contributor every thread fences again before reading
-    // all slots.
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int m = 2 * t + 8 * mt + (i & 1);
+                const int r = (warp * NT + nt) * 16 + g + 8 * (i >> 1);
+                if (m < p.M) base[(static_cast<int64_t>(slot) * p.M + m) * ROWS + r] = acc[nt][mt][i];
+            }
+    // Release: every thread orders its partial stores at gpu scope, the
+    // consumer warps meet, and one thread counts the CTA's arrival.
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
     named_bar_sync(1, CT);
-    if (tid == 0) *flag = (atomicAdd(&p.counters[blk], 1u) == static_cast<unsigned>(total - 1)) ? 1 : 0;
-    named_bar_sync(1, CT);
-    const bool is_last = *flag != 0;
-    named_bar_sync(1, CT);  // the flag is reused by the next segment
-    if (!is_last) return;
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    // The last contributor sums the slots in slot order.  Thread = (block
-    // row, parity of m); all loads of a batch of slots are issued before the
-    // ordered adds, so the combine costs a few L2 round trips.
-    constexpr int TPR = CT / ROWS;  // threads per block row
-    static_assert(TPR * ROWS == CT && (TPR == 1 || TPR == 2), "combine thread map");
-    constexpr int MH = (MT * 8 + TPR - 1) / TPR;  // activation rows per thread
-    constexpr int BATCH = 4;
-    const int row = tid % ROWS, m0 = tid / ROWS;
-    float v[MH];
-#pragma unroll
-    for (int j = 0; j < MH; ++j) v[j] = 0.0f;
-    for (int sl0 = 0; sl0 < total; sl0 += BATCH) {
-        float tmp[MH][BATCH];
-#pragma unroll
-        for (int j = 0; j < MH; ++j) {
-            const int m = m0 + TPR * j;
-#pragma unroll
-            for (int u = 0; u < BATCH; ++u)
-                tmp[j][u] = (m < p.M && sl0 + u < total)
-                                ? __ldcg(base + (static_cast<int64_t>(sl0 + u) * p.M + m) * ROWS + row)
-                                : 0.0f;
+    if (tid == 0) atomicAdd(&p.counters[blk], 1u);
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *a) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// Second phase (the launch is cooperative, so every CTA of the grid is
+// resident): for each block this CTA contributed to, wait until all its
+// contributors have published their slots, then sum the slots in slot order
+// for this CTA's share of the block's 16-row tiles and apply the epilogue.
+// The CTA finishing last resets the block's counters for the next launch.
+// The wait is bounded; on timeout the status word says TIMEOUT.
+template <int MT>
+__device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp, int lane, int tid,
+                               volatile int *abort) {
+    constexpr int CT = CONSUMERS * 32, TILES = ROWS / 16, BATCH = 8;
+    if (hi <= lo) return;
+    unsigned *done = p.counters + kMaxTiles / 2;
+    const int b_first = static_cast<int>(lo / p.spb), b_last = static_cast<int>((hi - 1) / p.spb);
+    for (int blk = b_first; blk <= b_last; ++blk) {
+        int first, total;
+        block_contributors(p, blk, first, total);
+        if (total == 1) continue;
+        const int slot = static_cast<int>(blockIdx.x) - first;
+        if (tid == 0) {
+            const uint64_t start = globaltimer();
+            while (ld_acquire_gpu(&p.counters[blk]) < static_cast<unsigned>(total)) {
+                if (*abort || globaltimer() - start > 2000000000ull) {
+                    *abort = 1;
+                    atomicExch(p.status, static_cast<unsigned>(DEV_TIMEOUT));
+                    break;
+                }
+                __nanosleep(64);
+            }
         }
+        named_bar_sync(1, CT);
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        const float *base = p.partial + static_cast<int64_t>(blk) * p.max_slots * p.M * ROWS;
+        const int t0 = slot * TILES / total, t1 = (slot + 1) * TILES / total;
+        const int row0 = t0 * 16, nrows = (t1 - t0) * 16;
+        const int chunks = (nrows + 31) / 32;
+        // Work unit = (32-row chunk, activation row m), one warp each.
+        for (int u = warp; u < chunks * p.M; u += CONSUMERS) {
+            const int chunk = u / p.M, m = u - chunk * p.M;
+            const int rr = chunk * 32 + lane;
+            const bool active = rr < nrows;
+            const int row = row0 + (active ? rr : 0);
+            const float *src = base + static_cast<int64_t>(m) * ROWS + row;
+            const int64_t slot_stride = static_cast<int64_t>(p.M) * ROWS;
+            float v = 0.0f;
+            for (int sl0 = 0; sl0 < total; sl0 += BATCH) {
+                float tmp[BATCH];
 #pragma unroll
-        for (int j = 0; j < MH; ++j)
+                for (int k = 0; k < BATCH; ++k) tmp[k] = __ldcg(src + min(sl0 + k, total - 1) * slot_stride);
 #pragma unroll
-            for (int u = 0; u < BATCH; ++u) v[j] += tmp[j][u];
+                for (int k = 0; k < BATCH; ++k)
+                    if (sl0 + k < total) v += tmp[k];
+            }
+            finish_row(p, m, static_cast<int64_t>(blk) * ROWS + row0 + rr, v, lane, active);
+        }
+        if (tid == 0 && atomicAdd(&done[blk], 1u) == static_cast<unsigned>(total - 1)) {
+            p.counters[blk] = 0u;
+            done[blk] = 0u;
+        }
     }
-#pragma unroll
-    for (int j = 0; j < MH; ++j) {
-        const int m = m0 + TPR * j;
-        if (m >= p.M) break;  // warp-uniform
-        finish_row(p, m, nb0 + row, v[j], lane);
-    }
-    if (tid == 0) atomicExch(&p.counters[blk], 0u);
 }
 
 template <int BITS, int MT>
@@ -352,7 +389,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t *empty = full + MAX_STAGES;
     uint64_t *xsfull = empty + MAX_STAGES;
     volatile int *abort = reinterpret_cast<volatile int *>(xsfull + MAX_STAGES);
-    volatile int *flag = abort + 1;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
@@ -387,10 +423,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 char *dst = ring + stage * Sh::BYTES;
                 mbar_arrive_expect_tx(&full[stage], Sh::BYTES);
                 const int kk = st * KPS;
-                tma_load_2d(dst, &wmap, &full[stage], kk * BITS / 32, blk * ROWS);
                 const int g8 = (kk / GROUP) & ~7;
-                tma_load_2d(dst + Sh::W, &smap, &full[stage], g8, blk * ROWS);
-                tma_load_2d(dst + Sh::W + Sh::SB, &bmap, &full[stage], g8, blk * ROWS);
+#pragma unroll
+                for (int bx = 0; bx < ROWS / BOX_ROWS; ++bx) {
+                    const int row0 = blk * ROWS + bx * BOX_ROWS;
+                    tma_load_2d(dst + bx * BOX_ROWS * 128, &wmap, &full[stage], kk * BITS / 32, row0);
+                    tma_load_2d(dst + Sh::W + bx * BOX_ROWS * 16, &smap, &full[stage], g8, row0);
+                    tma_load_2d(dst + Sh::W + Sh::SB + bx * BOX_ROWS * 16, &bmap, &full[stage], g8, row0);
+                }
 #pragma unroll
                 for (int G = 0; G < GPS; ++G)
                     tma_load_2d(dst + Sh::W + 2 * Sh::SB + G * X_BOX_BYTES, &xmap, &full[stage], kk + G * GROUP, 0);
@@ -442,14 +482,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         int stage = 0;
         uint32_t phase = 0;
         int64_t i = lo;
-        const int r0 = warp * 16 + g;  // block rows r0 and r0 + 8 of this thread
         while (i < hi) {
             const int blk = static_cast<int>(i / p.spb);
             const int64_t blk_begin = static_cast<int64_t>(blk) * p.spb;
             const int64_t seg_end = min(hi, blk_begin + p.spb);
-            uint64_t acc[MT][2];  // packed f32 pairs: [mt][0] = (c0, c1), [mt][1] = (c2, c3)
+            uint64_t acc[NT][MT][2];  // packed f32 pairs: [..][0] = (c0, c1), [..][1] = (c2, c3)
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = 0ull;
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) acc[nt][mt][0] = acc[nt][mt][1] = 0ull;
 
             for (; i < seg_end; ++i) {
                 const int j = static_cast<int>(i - blk_begin);  // stage index within the block
@@ -462,19 +503,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const char *bsb = ssb + Sh::SB;
                 const char *xsb = bsb + Sh::SB;
                 const int go0 = (j * GPS) & 7;  // first group of this stage within the 8-group scale box
-                uint32_t sv[2][GPS / 2], bv[2][GPS / 2];
+                uint32_t sv[NT][2][GPS / 2], bv[NT][2][GPS / 2];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int r = r0 + 8 * h;
-                    if constexpr (GPS == 4) {
-                        const uint2 a2 = *reinterpret_cast<const uint2 *>(ssb + r * 16 + go0 * 2);
-                        const uint2 b2 = *reinterpret_cast<const uint2 *>(bsb + r * 16 + go0 * 2);
-                        sv[h][0] = a2.x; sv[h][1] = a2.y; bv[h][0] = b2.x; bv[h][1] = b2.y;
-                    } else {
-                        sv[h][0] = *reinterpret_cast<const uint32_t *>(ssb + r * 16 + go0 * 2);
-                        bv[h][0] = *reinterpret_cast<const uint32_t *>(bsb + r * 16 + go0 * 2);
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int r = (warp * NT + nt) * 16 + g + 8 * h;
+                        if constexpr (GPS == 4) {
+                            const uint2 a2 = *reinterpret_cast<const uint2 *>(ssb + r * 16 + go0 * 2);
+                            const uint2 b2 = *reinterpret_cast<const uint2 *>(bsb + r * 16 + go0 * 2);
+                            sv[nt][h][0] = a2.x; sv[nt][h][1] = a2.y; bv[nt][h][0] = b2.x; bv[nt][h][1] = b2.y;
+                        } else {
+                            sv[nt][h][0] = *reinterpret_cast<const uint32_t *>(ssb + r * 16 + go0 * 2);
+                            bv[nt][h][0] = *reinterpret_cast<const uint32_t *>(bsb + r * 16 + go0 * 2);
+                        }
                     }
-                }
                 mbar_wait(&xsfull[stage], phase, abort, p.status);
                 const float *xs = xsums + stage * GPS * 16;
 #pragma unroll
@@ -492,63 +535,81 @@ __global__ void __launch_bounds__(THREADS, 1)
                         xf[mt][0] = v0.x; xf[mt][1] = v0.y; xf[mt][2] = v0.z; xf[mt][3] = v0.w;
                         xf[mt][4] = v1.x; xf[mt][5] = v1.y; xf[mt][6] = v1.z; xf[mt][7] = v1.w;
                     }
-                    // A fragments of all four k-steps first, then the MMAs with
-                    // the m-tiles interleaved (independent accumulator chains).
-                    uint32_t a[4][4];
-                    if constexpr (BITS == 4) {
-                        const int off = (((2 * G + (t >> 1)) ^ g) << 4) + (t & 1) * 8;
-                        const uint2 u0 = *reinterpret_cast<const uint2 *>(sw + r0 * 128 + off);
-                        const uint2 u1 = *reinterpret_cast<const uint2 *>(sw + (r0 + 8) * 128 + off);
-                        const uint32_t w0[2] = {u0.x, u0.y}, w1[2] = {u1.x, u1.y};
+                    // A fragments of both tiles and all four k-steps first, then
+                    // the MMAs with tiles and m-tiles interleaved (NT * MT
+                    // independent accumulator chains).
+                    uint32_t a[NT][4][4];
 #pragma unroll
-                        for (int s = 0; s < 4; ++s) {
-                            const int p0 = 2 * (s & 1);
-                            a[s][0] = dec4(w0[s >> 1], p0);
-                            a[s][1] = dec4(w1[s >> 1], p0);
-                            a[s][2] = dec4(w0[s >> 1], p0 + 1);
-                            a[s][3] = dec4(w1[s >> 1], p0 + 1);
-                        }
-                    } else {
-                        const int off = ((4 * G + t) ^ g) << 4;
-                        const uint4 u0 = *reinterpret_cast<const uint4 *>(sw + r0 * 128 + off);
-                        const uint4 u1 = *reinterpret_cast<const uint4 *>(sw + (r0 + 8) * 128 + off);
-                        const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const char *tw = sw + ((warp * NT + nt) * 16 + g) * 128;  // rows r and r + 8
+                        if constexpr (BITS == 4) {
+                            const int off = (((2 * G + (t >> 1)) ^ g) << 4) + (t & 1) * 8;
+                            const uint2 u0 = *reinterpret_cast<const uint2 *>(tw + off);
+                            const uint2 u1 = *reinterpret_cast<const uint2 *>(tw + 8 * 128 + off);
+                            const uint32_t w0[2] = {u0.x, u0.y}, w1[2] = {u1.x, u1.y};
 #pragma unroll
-                        for (int s = 0; s < 4; ++s) {
-                            a[s][0] = dec8(w0[s], 0);
-                            a[s][1] = dec8(w1[s], 0);
-                            a[s][2] = dec8(w0[s], 2);
-                            a[s][3] = dec8(w1[s], 2);
+                            for (int s = 0; s < 4; ++s) {
+                                const int p0 = 2 * (s & 1);
+                                a[nt][s][0] = dec4(w0[s >> 1], p0);
+                                a[nt][s][1] = dec4(w1[s >> 1], p0);
+                                a[nt][s][2] = dec4(w0[s >> 1], p0 + 1);
+                                a[nt][s][3] = dec4(w1[s >> 1], p0 + 1);
+                            }
+                        } else {
+                            const int off = ((4 * G + t) ^ g) << 4;
+                            const uint4 u0 = *reinterpret_cast<const uint4 *>(tw + off);
+                            const uint4 u1 = *reinterpret_cast<const uint4 *>(tw + 8 * 128 + off);
+                            const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+                            for (int s = 0; s < 4; ++s) {
+                                a[nt][s][0] = dec8(w0[s], 0);
+                                a[nt][s][1] = dec8(w1[s], 0);
+                                a[nt][s][2] = dec8(w0[s], 2);
+                                a[nt][s][3] = dec8(w1[s], 2);
+                            }
                         }
                     }
-                    float c[MT][4];
+                    float c[NT][MT][4];
 #pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) c[nt][mt][0] = c[nt][mt][1] = c[nt][mt][2] = c[nt][mt][3] = 0.f;
 #pragma unroll
                     for (int s = 0; s < 4; ++s)
 #pragma unroll
-                        for (int mt = 0; mt < MT; ++mt) {
-                            const uint32_t b0 = BITS == 4 ? xf[mt][4 * (s >> 1) + 2 * (s & 1)] : xf[mt][2 * s];
-                            const uint32_t b1 = BITS == 4 ? xf[mt][4 * (s >> 1) + 2 * (s & 1) + 1] : xf[mt][2 * s + 1];
-                            mma_bf16_16816(c[mt], a[s], b0, b1, c[mt]);
-                        }
-                    const uint32_t s_w0 = sv[0][G >> 1], s_w1 = sv[1][G >> 1];
-                    const uint32_t b_w0 = bv[0][G >> 1], b_w1 = bv[1][G >> 1];
-                    const float s0 = __uint_as_float((G & 1) ? (s_w0 & 0xFFFF0000u) : (s_w0 << 16));
-                    const float s1 = __uint_as_float((G & 1) ? (s_w1 & 0xFFFF0000u) : (s_w1 << 16));
-                    float q0 = __uint_as_float((G & 1) ? (b_w0 & 0xFFFF0000u) : (b_w0 << 16));
-                    float q1 = __uint_as_float((G & 1) ? (b_w1 & 0xFFFF0000u) : (b_w1 << 16));
-                    if constexpr (BITS == 4) {  // codes entered the MMA as 128+q
-                        q0 = fmaf(-128.0f, s0, q0);
-                        q1 = fmaf(-128.0f, s1, q1);
-                    }
-                    const uint64_t s0p = f2_pack(s0, s0), s1p = f2_pack(s1, s1);
-                    const uint64_t q0p = f2_pack(q0, q0), q1p = f2_pack(q1, q1);
+                        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) {
-                        const uint64_t xsum = *reinterpret_cast<const uint64_t *>(xs + G * 16 + 8 * mt + 2 * t);
-                        acc[mt][0] = fma_f32x2(s0p, f2_pack(c[mt][0], c[mt][1]), fma_f32x2(q0p, xsum, acc[mt][0]));
-                        acc[mt][1] = fma_f32x2(s1p, f2_pack(c[mt][2], c[mt][3]), fma_f32x2(q1p, xsum, acc[mt][1]));
+                            for (int mt = 0; mt < MT; ++mt) {
+                                const uint32_t b0 = BITS == 4 ? xf[mt][4 * (s >> 1) + 2 * (s & 1)] : xf[mt][2 * s];
+                                const uint32_t b1 =
+                                    BITS == 4 ? xf[mt][4 * (s >> 1) + 2 * (s & 1) + 1] : xf[mt][2 * s + 1];
+                                mma_bf16_16816(c[nt][mt], a[nt][s], b0, b1, c[nt][mt]);
+                            }
+                    uint64_t xsum[MT];
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt)
+                        xsum[mt] = *reinterpret_cast<const uint64_t *>(xs + G * 16 + 8 * mt + 2 * t);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const uint32_t s_w0 = sv[nt][0][G >> 1], s_w1 = sv[nt][1][G >> 1];
+                        const uint32_t b_w0 = bv[nt][0][G >> 1], b_w1 = bv[nt][1][G >> 1];
+                        const float s0 = __uint_as_float((G & 1) ? (s_w0 & 0xFFFF0000u) : (s_w0 << 16));
+                        const float s1 = __uint_as_float((G & 1) ? (s_w1 & 0xFFFF0000u) : (s_w1 << 16));
+                        float q0 = __uint_as_float((G & 1) ? (b_w0 & 0xFFFF0000u) : (b_w0 << 16));
+                        float q1 = __uint_as_float((G & 1) ? (b_w1 & 0xFFFF0000u) : (b_w1 << 16));
+                        if constexpr (BITS == 4) {  // codes entered the MMA as 128+q
+                            q0 = fmaf(-128.0f, s0, q0);
+                            q1 = fmaf(-128.0f, s1, q1);
+                        }
+                        const uint64_t s0p = f2_pack(s0, s0), s1p = f2_pack(s1, s1);
+                        const uint64_t q0p = f2_pack(q0, q0), q1p = f2_pack(q1, q1);
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            acc[nt][mt][0] = fma_f32x2(s0p, f2_pack(c[nt][mt][0], c[nt][mt][1]),
+                                                       fma_f32x2(q0p, xsum[mt], acc[nt][mt][0]));
+                            acc[nt][mt][1] = fma_f32x2(s1p, f2_pack(c[nt][mt][2], c[nt][mt][3]),
+                                                       fma_f32x2(q1p, xsum[mt], acc[nt][mt][1]));
+                        }
                     }
                 }
                 // The stage is refilled by TMA (async proxy) after this release;
@@ -558,16 +619,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (lane == 0) mbar_arrive(&empty[stage]);
                 if (++stage == S) { stage = 0; phase ^= 1; }
             }
-            float accf[MT][4];
+            float accf[NT][MT][4];
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                accf[mt][0] = __uint_as_float(static_cast<uint32_t>(acc[mt][0]));
-                accf[mt][1] = __uint_as_float(static_cast<uint32_t>(acc[mt][0] >> 32));
-                accf[mt][2] = __uint_as_float(static_cast<uint32_t>(acc[mt][1]));
-                accf[mt][3] = __uint_as_float(static_cast<uint32_t>(acc[mt][1] >> 32));
-            }
-            segment_epilogue<MT>(p, accf, blk, warp, g, t, lane, tid, flag);
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    accf[nt][mt][0] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][0]));
+                    accf[nt][mt][1] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][0] >> 32));
+                    accf[nt][mt][2] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][1]));
+                    accf[nt][mt][3] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][1] >> 32));
+                }
+            segment_epilogue<MT>(p, accf, blk, warp, g, t, tid);
         }
+        combine_blocks<MT>(p, lo, hi, warp, lane, tid, abort);
     }
 }
 
@@ -643,7 +707,7 @@ bool qmv_supported(const QmmArgs &a, const char **why) {
     if (!al(a.w.ptr, 16) || (a.w.row_stride * 4) % 16) return no("qmv: packed rows must be 16-byte aligned");
     if (!al(a.s.ptr, 16) || !al(a.b.ptr, 16) || (a.s.row_stride * 2) % 16 || (a.b.row_stride * 2) % 16)
         return no("qmv: parameter rows must be 16-byte aligned");
-    if ((a.N + qmv::ROWS - 1) / qmv::ROWS > kMaxTiles) return no("qmv: N beyond the arrival-counter region");
+    if ((a.N + qmv::ROWS - 1) / qmv::ROWS > kMaxTiles / 2) return no("qmv: N beyond the arrival-counter region");
     if (a.N >= (int64_t(1) << 31) || a.K >= (int64_t(1) << 30)) return no("qmv: size beyond 32-bit indexing");
     return true;
 }
@@ -666,7 +730,10 @@ QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     const int kps = a.bits == 4 ? 256 : 128;
     const int64_t spb = a.K / kps;
     const int64_t items = nblocks * spb;
-    const int grid = static_cast<int>(std::min<int64_t>(num_sms, items));
+    // The fewest CTAs with the makespan of one per SM: fewer contributors per
+    // block, less partial traffic.
+    const int64_t per_sm = (items + num_sms - 1) / num_sms;
+    const int grid = static_cast<int>((items + per_sm - 1) / per_sm);
     // Contributors per block: a block spans at most ceil(spb / floor(items/grid)) + 1 CTAs.
     const int64_t per_cta = std::max<int64_t>(1, items / grid);
     const int max_slots = static_cast<int>(std::min<int64_t>((spb + per_cta - 1) / per_cta + 1, grid));
@@ -699,9 +766,21 @@ static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, cons
     auto kern = qmv::qmv_kernel<BITS, MT>;
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(kern), plan.smem_bytes);
     if (e != cudaSuccess) return e;
-    kern<<<plan.grid_n, qmv::THREADS, plan.smem_bytes, stream>>>(wm, sm, bm, xm, p);
+    // Cooperative: every CTA is resident, so the combine phase may wait for
+    // the other contributors of a block.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(plan.grid_n);
+    cfg.blockDim = dim3(qmv::THREADS);
+    cfg.dynamicSmemBytes = plan.smem_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, wm, sm, bm, xm, p);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_qmv_prep(const void *src, int64_t ld_src, int mode, const float *ss, int ss_tiles,
@@ -752,11 +831,11 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     const CUtensorMap *wm, *sm, *bm, *xm;
     const uint64_t words = static_cast<uint64_t>(a.K) * a.bits / 32;
     if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32,
-                                    qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+                                    qmv::BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_128B)) ||
         !(sm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2, 8,
-                                    qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+                                    qmv::BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
         !(bm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2, 8,
-                                    qmv::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+                                    qmv::BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
         !(xm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xq, a.K, a.M, ldxq * 2, 64, 16,
                                     CU_TENSOR_MAP_SWIZZLE_128B)))
         return cudaErrorInvalidValue;
