@@ -11,7 +11,9 @@ LIB_PATH = HERE / "libaffon_b200.so"
 HEADER = HERE.parent / "include" / "affon_b200.h"
 
 OK, INVALID_SHAPE, UNSUPPORTED, CUDA_ERROR, TIMEOUT, GUARD_MISMATCH, POLICY_REJECTED, INVALID_ARG, INVALID_DTYPE = range(9)
-F32, BF16, U32 = 0, 1, 2
+F32, BF16, U32, U64 = 0, 1, 2, 3
+REDUCE_SUM, REDUCE_MAX = 0, 1
+TP_ID_BYTES = 144
 POLICY = {"backend_equivalent": 0, "exact_only": 1, "approximate": 2}
 NUMERICS = {0: "exact", 1: "reassociated", 2: "approximate"}
 
@@ -31,7 +33,7 @@ class QmmDesc(ctypes.Structure):
 class QmvFusion(ctypes.Structure):
     _fields_ = [("struct_size", c_u32), ("x_mode", c_i32), ("epilogue", c_i32), ("act_pair_order", c_i32),
                 ("h_out", c_vp), ("ld_h_out", c_i64), ("ss_out", c_vp), ("act", c_vp), ("ld_act", c_i64),
-                ("amax", c_vp)]
+                ("amax", c_vp), ("index_offset", c_i64)]
 
 
 class AttnDesc(ctypes.Structure):
@@ -42,6 +44,8 @@ class AttnDesc(ctypes.Structure):
 
 
 EPI_STORE, EPI_RESID, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
+SS_WIDTH = 32      # row width of the per-16-column sums of squares ([cols/16][SS_WIDTH] f32)
+MAX_QMV_ROWS = 32  # activation rows the decode qmv takes in one pass
 
 
 class Selection(ctypes.Structure):
@@ -68,13 +72,28 @@ SIGNATURES = {
     "affon_b200_compute_core_run_quantized_matmul_f32": ([c_vp, c_sz, c_vp, c_sz, c_vp, c_sz, c_vp, c_sz, c_vp, c_sz,
                                                           c_sz, c_sz, c_sz, c_sz, c_sz], c_i32),
     "affon_b200_qmv_noalloc": ([ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_qmv_noalloc_status": ([c_vp, ctypes.POINTER(c_u32)], c_i32),
+    "affon_b200_ctx_set_overlap": ([c_vp, c_i32], c_i32),
+    "affon_b200_debug_set_combine_wait": ([ctypes.c_uint64, c_u32], c_i32),
     "affon_b200_qmv_fused": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp,
                               ctypes.POINTER(QmvFusion)], c_i32),
     "affon_b200_qmv_prep": ([c_vp, c_i32, c_vp, c_i64, c_vp, c_i32, c_vp, ctypes.c_float, c_i32, c_i32, c_i32, c_vp,
                              c_i64], c_i32),
+    "affon_b200_resid_norm": ([c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, ctypes.c_float, c_i32, c_i32, c_i32, c_vp,
+                               c_i64], c_i32),
+    "affon_b200_tp_unique_id": ([c_vp], c_i32),
+    "affon_b200_tp_id_check": ([c_vp], c_i32),
+    "affon_b200_tp_init": ([c_vp, c_i32, c_i32, c_vp, ctypes.c_double], c_i32),
+    "affon_b200_tp_rank": ([c_vp], c_i32),
+    "affon_b200_tp_world": ([c_vp], c_i32),
+    "affon_b200_tp_allreduce": ([c_vp, c_vp, c_sz, c_i32, c_i32], c_i32),
+    "affon_b200_tp_allreduce_bf16": ([c_vp, c_vp, c_sz], c_i32),
+    "affon_b200_tp_synchronize": ([c_vp, ctypes.c_double], c_i32),
+    "affon_b200_tp_abort": ([c_vp], c_i32),
+    "affon_b200_tp_destroy": ([c_vp], c_i32),
     "affon_b200_decode_attention": ([c_vp, ctypes.POINTER(AttnDesc), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
-    "affon_b200_embed": ([c_vp, c_vp, c_i64, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp], c_i32),
-    "affon_b200_argmax_finalize": ([c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_embed": ([c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_argmax_finalize": ([c_vp, c_vp, c_i32, c_vp, c_vp, c_i32, c_vp, c_vp], c_i32),
     "affon_b200_launch_count": ([], ctypes.c_uint64),
 }
 

@@ -9,17 +9,8 @@
 
 #include "../../include/affon_b200.h"
 #include "internal.h"
+#include "sm100.cuh"
 
-struct affon_b200_ctx {
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    int num_sms = 148;
-    void *workspace = nullptr;
-    size_t workspace_bytes = 0;
-    // Staging buffers of the host-buffer entry points (grown on demand).
-    void *stage[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
-    size_t stage_bytes[5] = {0, 0, 0, 0, 0};
-};
 
 namespace afb {
 
@@ -156,7 +147,7 @@ enum Impl { IMPL_GENERIC = 0, IMPL_QMV = 1, IMPL_QMM_TC = 2 };
 struct Choice {
     Impl impl;
     afb::QmvPlan plan;
-    int passes;  // qmv passes over 16-row slices of M
+    int passes;  // qmv passes over 32-row slices of M
 };
 
 int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms, size_t workspace,
@@ -170,7 +161,7 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
     char reason[256];
     const char *why_qmv = "";
     afb::QmmArgs probe = a;
-    probe.M = a.M < 16 ? a.M : 16;
+    probe.M = a.M < afb::kMaxQmvRows ? a.M : afb::kMaxQmvRows;
     const bool qmv_ok = afb::qmv_supported(probe, &why_qmv);
     const char *why_tc = "";
     const bool tc_ok = afb::qmm_tc_supported(a, &why_tc);
@@ -178,20 +169,20 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
     if (qmv_ok) qplan = afb::qmv_plan(probe, num_sms, workspace);
     const bool qmv_plannable = qmv_ok && qplan.splits > 0;
     if (qmv_ok && !qmv_plannable) why_qmv = "qmv: no split fits shared memory and the context workspace";
-    if (qmv_plannable && a.M <= 16) {
+    if (qmv_plannable && a.M <= afb::kMaxQmvRows) {
         c.impl = IMPL_QMV;
         c.plan = qplan;
         snprintf(reason, sizeof reason,
-                 "M=%lld <= 16: decode qmv, stream-K over %d CTAs, up to %d K segments per tile, %d-stage ring",
+                 "M=%lld <= 32: decode qmv, stream-K over %d CTAs, up to %d K segments per tile, %d-stage ring",
                  (long long)a.M, c.plan.grid_n, c.plan.max_slots, c.plan.stages);
     } else if (tc_ok && (d->numerical_policy == AFFON_B200_POLICY_APPROXIMATE || a.y_bf16)) {
         c.impl = IMPL_QMM_TC;
         snprintf(reason, sizeof reason, "M=%lld >= 64: tcgen05 qmm with bf16-rounded decoded weights", (long long)a.M);
     } else if (qmv_plannable && (a.M <= 64 || d->numerical_policy != AFFON_B200_POLICY_APPROXIMATE)) {
         c.impl = IMPL_QMV;
-        c.passes = static_cast<int>((a.M + 15) / 16);
+        c.passes = static_cast<int>((a.M + afb::kMaxQmvRows - 1) / afb::kMaxQmvRows);
         c.plan = qplan;
-        snprintf(reason, sizeof reason, "M=%lld > 16: %d qmv passes over 16-row slices", (long long)a.M, c.passes);
+        snprintf(reason, sizeof reason, "M=%lld > 32: %d qmv passes over 32-row slices", (long long)a.M, c.passes);
     } else {
         snprintf(reason, sizeof reason, "generic strided kernel (%s%s%s)", why_qmv, tc_ok ? "" : "; ",
                  tc_ok ? "" : why_tc);
@@ -221,15 +212,16 @@ int launch(affon_b200_ctx *ctx, const afb::QmmArgs &a, const Choice &c) {
     case IMPL_QMV: {
         for (int pass = 0; pass < c.passes && e == cudaSuccess; ++pass) {
             afb::QmmArgs slice = a;
-            const int64_t m0 = int64_t(pass) * 16;
-            slice.M = (a.M - m0) < 16 ? (a.M - m0) : 16;
+            const int64_t m0 = int64_t(pass) * afb::kMaxQmvRows;
+            slice.M = (a.M - m0) < afb::kMaxQmvRows ? (a.M - m0) : afb::kMaxQmvRows;
             slice.x.ptr = static_cast<const char *>(a.x.ptr) + m0 * a.x.row_stride * 2;
             slice.y = static_cast<char *>(a.y) + m0 * a.ldy * (a.y_bf16 ? 2 : 4);
-            afb::QmvPlan plan = slice.M == 16 || c.passes == 1 ? c.plan
-                                                                : afb::qmv_plan(slice, ctx->num_sms, ctx->workspace_bytes);
-            if (afb::qmv_workspace_bytes(slice, plan) > ctx->workspace_bytes)
+            afb::QmvPlan plan = slice.M == afb::kMaxQmvRows || c.passes == 1
+                                    ? c.plan
+                                    : afb::qmv_plan(slice, ctx->num_sms, ctx->workspace_bytes);
+            if (plan.splits < 1 || afb::qmv_workspace_bytes(slice, plan) > ctx->workspace_bytes)
                 return fail(AFFON_B200_CUDA_ERROR, "qmv plan exceeds the context workspace");
-            e = afb::launch_qmv(slice, plan, ctx->workspace, ctx->stream);
+            e = afb::launch_qmv(slice, plan, ctx->workspace, ctx->stream, nullptr, ctx->overlap);
         }
         break;
     }
@@ -313,6 +305,7 @@ int affon_b200_ctx_destroy(affon_b200_ctx *ctx) {
     DeviceGuard guard(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     else cudaDeviceSynchronize();
+    if (ctx->tp) afb::tp_release(ctx);
     if (ctx->workspace) cudaFree(ctx->workspace);
     for (void *p : ctx->stage)
         if (p) cudaFree(p);
@@ -328,6 +321,17 @@ int affon_b200_ctx_set_stream(affon_b200_ctx *ctx, void *cuda_stream) {
 }
 
 int affon_b200_ctx_device(const affon_b200_ctx *ctx) { return ctx ? ctx->device : -1; }
+
+int affon_b200_ctx_set_overlap(affon_b200_ctx *ctx, int enable) {
+    if (!ctx) return fail(AFFON_B200_INVALID_ARG, "null context");
+    ctx->overlap = enable != 0;
+    return AFFON_B200_OK;
+}
+
+int affon_b200_debug_set_combine_wait(uint64_t limit_ns, uint32_t extra_arrivals) {
+    afb::qmv_set_combine_wait(limit_ns, extra_arrivals);
+    return AFFON_B200_OK;
+}
 
 int affon_b200_ctx_reserve_workspace(affon_b200_ctx *ctx, size_t bytes) {
     if (!ctx) return fail(AFFON_B200_INVALID_ARG, "null context");
@@ -361,7 +365,12 @@ int affon_b200_ctx_synchronize(affon_b200_ctx *ctx) {
     if (status != 0) {
         // A kernel that gave up may have left arrival counters behind: clear
         // the status word and the whole counter region for the next launch.
-        cudaMemset(ctx->workspace, 0, afb::kPartialOffset);
+        if ((e = cudaMemset(ctx->workspace, 0, afb::kPartialOffset)) != cudaSuccess ||
+            (e = cudaDeviceSynchronize()) != cudaSuccess)
+            return cuda_fail(e, "status reset");
+        if (status == afb::DEV_BOUNDS)
+            return fail(AFFON_B200_INVALID_ARG,
+                        "a kernel read a position or token outside its buffer and skipped it (device status %u)", status);
         return fail(AFFON_B200_TIMEOUT, "a kernel gave up a bounded wait (device status %u)", status);
     }
     return AFFON_B200_OK;
@@ -461,6 +470,7 @@ int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, c
     f.ld_act = fusion->ld_act;
     f.act_pair_order = fusion->act_pair_order;
     f.amax = fusion->amax;
+    f.index_offset = fusion->index_offset;
     if (f.x_mode != 0 && f.x_mode != 1) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: x_mode must be 0 or 1");
     if (f.epi < 0 || f.epi > 3) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: unknown epilogue");
     if ((f.epi == 1 && (!f.h_out || !f.ss_out)) || (f.epi == 2 && !f.act) || (f.epi == 3 && !f.amax) ||
@@ -475,7 +485,7 @@ int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, c
     const afb::QmvPlan plan = afb::qmv_plan(a, ctx->num_sms, ctx->workspace_bytes);
     if (plan.splits < 1) return fail(AFFON_B200_UNSUPPORTED, "qmv_fused: no plan fits the context workspace");
     DeviceGuard guard(ctx->device);
-    cudaError_t e = afb::launch_qmv(a, plan, ctx->workspace, ctx->stream, &f);
+    cudaError_t e = afb::launch_qmv(a, plan, ctx->workspace, ctx->stream, &f, ctx->overlap);
     if (e != cudaSuccess) return cuda_fail(e, "qmv_fused launch");
     return AFFON_B200_OK;
 }
@@ -484,7 +494,7 @@ int affon_b200_qmv_prep(affon_b200_ctx *ctx, int mode, const void *src, int64_t 
                         int ss_tiles, const void *gamma, float eps, int rows, int cols, int bits, void *dst,
                         int64_t ld_dst) {
     t_error.clear();
-    if (!ctx || !src || !dst || rows <= 0 || rows > 16 || cols <= 0 || cols % 8 || (bits != 4 && bits != 8) ||
+    if (!ctx || !src || !dst || rows <= 0 || rows > afb::kMaxQmvRows || cols <= 0 || cols % 8 || (bits != 4 && bits != 8) ||
         (mode != 0 && mode != 1) || ld_src % 8 || ld_dst % 8)
         return fail(AFFON_B200_INVALID_ARG, "qmv_prep: bad arguments");
     if (mode == 1 && (!ss || !gamma || ss_tiles <= 0))
@@ -493,8 +503,25 @@ int affon_b200_qmv_prep(affon_b200_ctx *ctx, int mode, const void *src, int64_t 
     if (!al16(src) || !al16(dst) || (gamma && !al16(gamma))) return fail(AFFON_B200_INVALID_ARG, "qmv_prep: alignment");
     DeviceGuard guard(ctx->device);
     cudaError_t e = afb::launch_qmv_prep(src, ld_src, mode, ss, ss_tiles, static_cast<const uint16_t *>(gamma), eps,
-                                         rows, cols, bits, static_cast<uint16_t *>(dst), ld_dst, ctx->stream);
+                                         rows, cols, bits, static_cast<uint16_t *>(dst), ld_dst, ctx->stream,
+                                         ctx->overlap);
     if (e != cudaSuccess) return cuda_fail(e, "qmv_prep launch");
+    return AFFON_B200_OK;
+}
+
+int affon_b200_resid_norm(affon_b200_ctx *ctx, float *h, int64_t ld_h, const float *add, int64_t ld_add,
+                          const void *gamma, float eps, int rows, int cols, int bits, void *dst, int64_t ld_dst) {
+    t_error.clear();
+    if (!ctx || !h || !gamma || !dst || rows <= 0 || rows > afb::kMaxQmvRows || cols <= 0 || cols % 8 ||
+        cols > 8192 || (bits != 4 && bits != 8) || ld_h % 4 || (add && ld_add % 4) || ld_dst % 8)
+        return fail(AFFON_B200_INVALID_ARG, "resid_norm: bad arguments (rows <= 32, cols % 8 == 0, cols <= 8192)");
+    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) % 16) == 0; };
+    if (!al16(h) || (add && !al16(add)) || !al16(gamma) || !al16(dst))
+        return fail(AFFON_B200_INVALID_ARG, "resid_norm: alignment");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = afb::launch_resid_norm(h, ld_h, add, ld_add, static_cast<const uint16_t *>(gamma), eps, rows, cols,
+                                           bits, static_cast<uint16_t *>(dst), ld_dst, ctx->stream, ctx->overlap);
+    if (e != cudaSuccess) return cuda_fail(e, "resid_norm launch");
     return AFFON_B200_OK;
 }
 
@@ -511,9 +538,8 @@ int affon_b200_decode_attention(affon_b200_ctx *ctx, const affon_b200_attn_desc 
         return fail(AFFON_B200_UNSUPPORTED, "decode_attention: head_dim 128 and 4 or 8 query heads per KV head");
     if ((reinterpret_cast<uintptr_t>(k_cache) % 16) || (reinterpret_cast<uintptr_t>(v_cache) % 16))
         return fail(AFFON_B200_INVALID_ARG, "decode_attention: caches must be 16-byte aligned");
-    const size_t need = afb::kPartialOffset + size_t(d->batch) * d->kv_heads * ((d->capacity + 127) / 128) *
-                                                  (d->q_heads / d->kv_heads) * (128 + 2) * 4;
-    if (need > ctx->workspace_bytes || size_t(d->batch) * d->kv_heads > size_t(afb::kMaxTiles))
+    const size_t need = afb::attention_workspace_bytes(d->batch, d->kv_heads, d->q_heads, d->capacity, ctx->num_sms);
+    if (need > ctx->workspace_bytes || size_t(d->batch) * d->kv_heads > size_t(afb::kMaxTiles / 2))
         return fail(AFFON_B200_UNSUPPORTED, "decode_attention: partials exceed the context workspace");
     afb::DecodeAttnArgs a{};
     a.qkv = qkv;
@@ -536,29 +562,32 @@ int affon_b200_decode_attention(affon_b200_ctx *ctx, const affon_b200_attn_desc 
     a.scale = d->scale;
     a.out_pair_order = d->out_pair_order;
     DeviceGuard guard(ctx->device);
-    cudaError_t e = afb::launch_decode_attention(a, ctx->workspace, ctx->stream);
+    cudaError_t e = afb::launch_decode_attention(a, ctx->workspace, ctx->num_sms, ctx->stream, ctx->overlap);
     if (e != cudaSuccess) return cuda_fail(e, "decode_attention launch");
     return AFFON_B200_OK;
 }
 
-int affon_b200_embed(affon_b200_ctx *ctx, const void *table, int64_t ld_table, const int *tokens, int batch, int dim,
-                     float *h, float *ss_out, unsigned long long *amax) {
+int affon_b200_embed(affon_b200_ctx *ctx, const void *table, int64_t ld_table, int64_t vocab, const int *tokens,
+                     int batch, int dim, float *h, float *ss_out, unsigned long long *amax) {
     t_error.clear();
-    if (!ctx || !table || !tokens || !h || !ss_out || !amax || batch <= 0 || batch > 16 || dim <= 0 || dim % 16)
-        return fail(AFFON_B200_INVALID_ARG, "embed: bad arguments (batch <= 16, dim % 16 == 0)");
+    if (!ctx || !table || !tokens || !h || !ss_out || !amax || batch <= 0 || batch > afb::kMaxQmvRows || dim <= 0 ||
+        dim % 16 || vocab <= 0)
+        return fail(AFFON_B200_INVALID_ARG, "embed: bad arguments (batch <= 32, dim % 16 == 0, vocab > 0)");
     DeviceGuard guard(ctx->device);
-    cudaError_t e = afb::launch_embed(table, ld_table, tokens, batch, dim, h, ss_out, amax, ctx->stream);
+    cudaError_t e = afb::launch_embed(table, ld_table, vocab, tokens, batch, dim, h, ss_out, amax, ctx->workspace,
+                                      ctx->stream, ctx->overlap);
     if (e != cudaSuccess) return cuda_fail(e, "embed launch");
     return AFFON_B200_OK;
 }
 
 int affon_b200_argmax_finalize(affon_b200_ctx *ctx, const unsigned long long *amax, int batch, int *tokens,
-                               int *history, int *pos, int *step) {
+                               int *history, int history_rows, int *pos, int *step) {
     t_error.clear();
-    if (!ctx || !amax || !tokens || !pos || !step || batch <= 0 || batch > 1024)
+    if (!ctx || !amax || !tokens || !pos || !step || batch <= 0 || batch > 1024 || (history && history_rows <= 0))
         return fail(AFFON_B200_INVALID_ARG, "argmax_finalize: bad arguments");
     DeviceGuard guard(ctx->device);
-    cudaError_t e = afb::launch_finalize(amax, batch, tokens, history, pos, step, ctx->stream);
+    cudaError_t e = afb::launch_finalize(amax, batch, tokens, history, history_rows, pos, step, ctx->stream,
+                                         ctx->overlap);
     if (e != cudaSuccess) return cuda_fail(e, "finalize launch");
     return AFFON_B200_OK;
 }

@@ -6,14 +6,23 @@
 // kernels make the BASELINE decoder configurations runnable around the
 // quantized_matmul kernels.
 //
-// Decode attention, one CTA per (128-position chunk, KV head, batch row):
-// TMA loads the chunk's K and V rows (two 64-column boxes each, 128-byte
-// swizzle) while the CTA rotates its GQA group's queries.  The CTA holding the
-// current position also rotates the new key, writes key and value into the
-// cache (bf16) and uses them directly.  Scores and softmax are f32 on the CUDA
-// cores; each CTA leaves (max, sum, unnormalised output) per head, and the
-// last CTA of a (batch, KV head) -- per-pair arrival counter -- merges the
-// chunks in chunk order, so the result does not depend on scheduling.
+// Decode attention (flash-decoding).  Grid (splits, KV head, batch row): each
+// CTA takes an equal share of the context's 64-position tiles and streams
+// them through a 3-stage ring filled by TMA (K and V, two 64-column boxes
+// each, 128-byte swizzle).  Four consumer warps each own 16 positions of every
+// tile and run both products on tensor cores (mma.sync m16n8k16, bf16 in, f32
+// accumulate): S = Q K^T with the GQA group's G <= 8 query heads as the rows
+// of the A operand (pre-rotated, pre-scaled by log2(e)/sqrt(d), rounded to
+// bf16) and K fragments read with ldmatrix; an online softmax per warp in f32
+// (exp2); the probabilities, rounded to bf16, go from the S accumulators
+// straight into the A operand of O += P V, with V fragments from
+// ldmatrix.trans.  The warps' (max, sum, O) are merged in shared memory; when
+// the context is split over several CTAs, each writes its record and the last
+// CTA of the (batch, KV head) pair -- an arrival counter, nobody waits --
+// merges the records in split order, so the result does not depend on
+// scheduling.  The CTA holding the current position rotates the new key,
+// writes key and value into the cache (bf16) and patches them into its staged
+// tile, since the tile's TMA may have read the old row.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -23,10 +32,15 @@
 namespace afb {
 namespace dec {
 
-constexpr int HD = 128;        // head dimension
-constexpr int CH = 128;        // positions per chunk (CTA)
-constexpr int THREADS = 128;
-constexpr int BOX_BYTES = CH * 64 * 2;  // one 64-column half of a K or V chunk
+constexpr int HD = 128;                    // head dimension
+constexpr int TILE = 64;                   // positions per ring stage
+constexpr int STAGES = 3;
+constexpr int CWARPS = 4;                  // consumer warps, 16 positions of each tile each
+constexpr int THREADS = 32 * (CWARPS + 1);  // + one producer warp
+constexpr int BOX = TILE * 128;            // one 64-column half of a K or V tile: 8 KB
+constexpr int STAGE_BYTES = 4 * BOX;       // K lo, K hi, V lo, V hi
+constexpr int MAX_SPLITS = 16;
+constexpr float LOG2E = 1.4426950408889634f;
 
 struct AttnParams {
     const uint16_t *qkv;
@@ -37,212 +51,330 @@ struct AttnParams {
     const int *pos;
     uint16_t *out;
     int64_t ld_out;
-    float *partial;
-    unsigned *counters;
+    float *partial;                // [pair][split][G * (HD + 2)]
+    unsigned *counters;            // [pair]
     unsigned *status;
-    int B, QH, KVH, cap, max_chunks;
+    int B, QH, KVH, cap, splits;
     float scale;
     int out_pair_order;
 };
+
+// Byte offset of (row r, column c) of a 64-row x 128-dim bf16 tile stored as
+// two 64-column boxes with the 128-byte swizzle.
+__device__ __forceinline__ int tile_off(int r, int c) {
+    return (c >> 6) * BOX + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2;
+}
+
+__device__ __forceinline__ int out_column(int d, int pair_order) {
+    const int e = d & 7;
+    return pair_order ? (d & ~7) + (e < 4 ? 2 * e : 2 * (e - 4) + 1) : d;
+}
 
 template <int G>
 __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                    const __grid_constant__ CUtensorMap vmap,
                                                                    AttnParams p) {
     extern __shared__ char smem_raw[];
-    char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    char *ks = smem;                        // 2 boxes
-    char *vs = ks + 2 * BOX_BYTES;          // 2 boxes
-    float *qs = reinterpret_cast<float *>(vs + 2 * BOX_BYTES);  // [G][HD]
-    float *ps = qs + G * HD;                // [G][CH]
-    float *knew = ps + G * CH;              // [HD]
-    float *vnew = knew + HD;                // [HD]
-    float *stat = vnew + HD;                // m[G], l[G]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(stat + 2 * G + 2);
-    volatile int *flag = reinterpret_cast<volatile int *>(bar + 1);
+    char *ring = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + STAGES * STAGE_BYTES);
+    uint64_t *empty = full + STAGES;
+    volatile int *flag = reinterpret_cast<volatile int *>(empty + STAGES);
+    volatile int *abort = flag + 1;
+    // After the tile loop the ring holds the warps' records: m, l [CWARPS][8], o [CWARPS][8][HD].
+    float *red_m = reinterpret_cast<float *>(ring);
+    float *red_l = red_m + CWARPS * 8;
+    float *red_o = red_l + CWARPS * 8;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    pdl_launch_dependents();
+    pdl_wait();  // q/k/v and the position come from the preceding kernels
     const int pos = *p.pos;
-    const int n_chunks = pos / CH + 1;
-    if (c >= n_chunks) return;
-    const int c0 = c * CH;
-    const int len = min(CH, pos + 1 - c0);
-    const int row0 = (b * p.KVH + kvh) * p.cap + c0;
+    if (pos < 0 || pos >= p.cap) {  // no store, no TMA: report and leave
+        if (tid == 0 && split == 0 && kvh == 0 && b == 0) atomicExch(p.status, static_cast<unsigned>(DEV_BOUNDS));
+        return;
+    }
+    const int T = pos / TILE + 1;  // tiles holding positions 0..pos
+    const int t0 = split * T / p.splits, t1 = (split + 1) * T / p.splits;
+    const int64_t row_base = static_cast<int64_t>(b * p.KVH + kvh) * p.cap;
+    const int pair = b * p.KVH + kvh;
 
     if (tid == 0) {
-        mbar_init(bar, 1);
-        fence_mbar_init();
-        mbar_arrive_expect_tx(bar, 4 * BOX_BYTES);
-        tma_load_2d(ks, &kmap, bar, 0, row0);
-        tma_load_2d(ks + BOX_BYTES, &kmap, bar, 64, row0);
-        tma_load_2d(vs, &vmap, bar, 0, row0);
-        tma_load_2d(vs + BOX_BYTES, &vmap, bar, 64, row0);
-    }
-    // Rotated, pre-scaled queries of the GQA group (rotate-half RoPE: pairs
-    // (d, d+64) with angle pos * theta^(-2d/HD)).
-    const uint16_t *qrow = p.qkv + b * p.ld_qkv + p.q_off + kvh * G * HD;
-    const float *cs = p.cos_t + static_cast<int64_t>(pos) * (HD / 2), *sn = p.sin_t + static_cast<int64_t>(pos) * (HD / 2);
-    for (int i = tid; i < G * (HD / 2); i += THREADS) {
-        const int h = i / (HD / 2), d = i % (HD / 2);
-        const float a = bf16_bits_to_f32(qrow[h * HD + d]), bb = bf16_bits_to_f32(qrow[h * HD + d + HD / 2]);
-        qs[h * HD + d] = (a * cs[d] - bb * sn[d]) * p.scale;
-        qs[h * HD + d + HD / 2] = (bb * cs[d] + a * sn[d]) * p.scale;
-    }
-    const bool has_new = (pos >= c0) && (pos < c0 + CH);
-    if (has_new) {  // rotate the new key, write key and value rows into the cache
-        const uint16_t *krow = p.qkv + b * p.ld_qkv + p.k_off + kvh * HD;
-        const uint16_t *vrow = p.qkv + b * p.ld_qkv + p.v_off + kvh * HD;
-        const int64_t crow = static_cast<int64_t>((b * p.KVH + kvh) * p.cap + pos) * HD;
-        if (tid < HD / 2) {
-            const int d = tid;
-            const float a = bf16_bits_to_f32(krow[d]), bb = bf16_bits_to_f32(krow[d + HD / 2]);
-            const uint16_t r0 = f32_to_bf16_bits(a * cs[d] - bb * sn[d]);
-            const uint16_t r1 = f32_to_bf16_bits(bb * cs[d] + a * sn[d]);
-            p.kc[crow + d] = r0;
-            p.kc[crow + d + HD / 2] = r1;
-            knew[d] = bf16_bits_to_f32(r0);
-            knew[d + HD / 2] = bf16_bits_to_f32(r1);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], CWARPS);
         }
-        const uint16_t v = vrow[tid];
-        p.vc[crow + tid] = v;
-        vnew[tid] = bf16_bits_to_f32(v);
+        *abort = 0;
+        fence_mbar_init();
     }
     __syncthreads();
-    volatile int abort_flag = 0;
-    mbar_wait(bar, 0, &abort_flag, p.status);
 
-    // Scores: thread i <-> position c0 + i.  Row i of a box holds 64 columns in
-    // 16-byte chunks stored at chunk ^ (i % 8).
-    float sc[G];
+    if (warp == CWARPS) {  // ------------------------------------------ producer
+        if (lane == 0 && t1 > t0) {
+            tma_prefetch_desc(&kmap);
+            tma_prefetch_desc(&vmap);
+            int stage = 0;
+            uint32_t phase = 0, issued = 0, par = 0;
+            for (int i = t0; i < t1; ++i) {
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) break;
+                char *dst = ring + stage * STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+                const int row = static_cast<int>(row_base) + i * TILE;
+                tma_load_2d(dst, &kmap, &full[stage], 0, row);
+                tma_load_2d(dst + BOX, &kmap, &full[stage], 64, row);
+                tma_load_2d(dst + 2 * BOX, &vmap, &full[stage], 0, row);
+                tma_load_2d(dst + 3 * BOX, &vmap, &full[stage], 64, row);
+                issued |= 1u << stage;
+                par = (par & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            }
+            for (int s = 0; s < STAGES; ++s)
+                if (issued & (1u << s)) mbar_wait_drain(&full[s], (par >> s) & 1u);
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    const int g = lane >> 2, t = lane & 3;
+    // Q fragments: A rows = query heads (rows g < G; rows g + 8 stay zero),
+    // k-step ks covers dims 16 ks .. 16 ks + 15: a0 = dims 16ks+2t..+1,
+    // a2 = dims 16ks+2t+8..+9.  RoPE pairs (d, d + 64).
+    uint32_t qa[8][2];
+    {
+        const float qs = p.scale * LOG2E;
+        const uint16_t *qrow = p.qkv + b * p.ld_qkv + p.q_off + (kvh * G + (g < G ? g : 0)) * HD;
+        const float *cs = p.cos_t + static_cast<int64_t>(pos) * (HD / 2);
+        const float *sn = p.sin_t + static_cast<int64_t>(pos) * (HD / 2);
+        auto rot = [&](int d) {
+            const int dd = d & 63;
+            const float a = bf16_bits_to_f32(qrow[dd]), c = bf16_bits_to_f32(qrow[dd + 64]);
+            return (d < 64 ? a * cs[dd] - c * sn[dd] : c * cs[dd] + a * sn[dd]) * qs;
+        };
 #pragma unroll
-    for (int h = 0; h < G; ++h) sc[h] = -INFINITY;
-    if (tid < len) {
+        for (int ks = 0; ks < 8; ++ks) {
+            const int d0 = 16 * ks + 2 * t;
+            qa[ks][0] = g < G ? pack_bf16x2(rot(d0), rot(d0 + 1)) : 0u;
+            qa[ks][1] = g < G ? pack_bf16x2(rot(d0 + 8), rot(d0 + 9)) : 0u;
+        }
+    }
+    float m_run = -INFINITY, l_run = 0.0f;  // row g: running max (log2 units) and this thread's share of the sum
+    float o[16][4];
 #pragma unroll
-        for (int h = 0; h < G; ++h) sc[h] = 0.0f;
-        const bool fresh = (c0 + tid == pos);
-        for (int j = 0; j < HD / 8; ++j) {
-            float kv[8];
-            if (fresh) {
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+
+    const int i_new = pos / TILE, r_new = pos % TILE;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int i = t0; i < t1; ++i) {
+        mbar_wait(&full[stage], phase, abort, p.status);
+        char *tile = ring + stage * STAGE_BYTES;
+        if (i == i_new && warp == r_new / 16) {
+            // The current position: rotate the new key, store key and value
+            // (bf16) into the cache and into the staged tile.
+            const uint16_t *krow = p.qkv + b * p.ld_qkv + p.k_off + kvh * HD;
+            const uint16_t *vrow = p.qkv + b * p.ld_qkv + p.v_off + kvh * HD;
+            const float *cs = p.cos_t + static_cast<int64_t>(pos) * (HD / 2);
+            const float *sn = p.sin_t + static_cast<int64_t>(pos) * (HD / 2);
+            uint16_t *kdst = p.kc + (row_base + pos) * HD, *vdst = p.vc + (row_base + pos) * HD;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) kv[e] = knew[j * 8 + e];
-            } else {
-                const char *box = ks + (j >> 3) * BOX_BYTES;
-                const uint4 u = *reinterpret_cast<const uint4 *>(box + tid * 128 + (((j & 7) ^ (tid & 7)) << 4));
-                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    kv[2 * e] = __uint_as_float(w[e] << 16);
-                    kv[2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
-                }
+            for (int e = 0; e < 2; ++e) {
+                const int d = 2 * lane + e;  // 0..63
+                const float a = bf16_bits_to_f32(krow[d]), c = bf16_bits_to_f32(krow[d + 64]);
+                const uint16_t r0 = f32_to_bf16_bits(a * cs[d] - c * sn[d]);
+                const uint16_t r1 = f32_to_bf16_bits(c * cs[d] + a * sn[d]);
+                kdst[d] = r0;
+                kdst[d + 64] = r1;
+                *reinterpret_cast<uint16_t *>(tile + tile_off(r_new, d)) = r0;
+                *reinterpret_cast<uint16_t *>(tile + tile_off(r_new, d + 64)) = r1;
             }
 #pragma unroll
-            for (int h = 0; h < G; ++h)
+            for (int e = 0; e < 4; ++e) {
+                const int d = 4 * lane + e;
+                const uint16_t v = vrow[d];
+                vdst[d] = v;
+                *reinterpret_cast<uint16_t *>(tile + 2 * BOX + tile_off(r_new, d)) = v;
+            }
+            __syncwarp();
+        }
+        // S = Q K^T for this warp's 16 positions (n-tiles of 8).
+        const uint32_t kbase = smem_u32(tile), vbase = smem_u32(tile + 2 * BOX);
+        float sc[2][4];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) sc[h] = fmaf(qs[h * HD + j * 8 + e], kv[e], sc[h]);
+        for (int j = 0; j < 2; ++j) {
+            sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+            const int r = warp * 16 + j * 8 + (lane & 7);
+#pragma unroll
+            for (int kp = 0; kp < 4; ++kp) {  // k-steps 2kp, 2kp+1 = dims 32kp .. 32kp+31
+                const int c = 32 * kp + 8 * (lane >> 3);  // first dim of this lane's 8x8 matrix
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kbase + (c >> 6) * BOX + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4), b0, b1, b2, b3);
+                const uint32_t a0[4] = {qa[2 * kp][0], 0u, qa[2 * kp][1], 0u};
+                const uint32_t a1[4] = {qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u};
+                mma_bf16_16816(sc[j], a0, b0, b1, sc[j]);
+                mma_bf16_16816(sc[j], a1, b2, b3, sc[j]);
+            }
+        }
+        // Online softmax of row g over the 4 scores this thread holds.
+        const int p0 = i * TILE + warp * 16 + 2 * t;
+        float v[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
+        const int pp[4] = {p0, p0 + 1, p0 + 8, p0 + 9};
+        float mx = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (pp[e] > pos) v[e] = -INFINITY;
+            mx = fmaxf(mx, v[e]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float corr = m_new == -INFINITY ? 1.0f : exp2f(m_run - m_new);
+        float pr[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pr[e] = v[e] == -INFINITY ? 0.0f : exp2f(v[e] - m_new);
+        l_run = l_run * corr + (pr[0] + pr[1]) + (pr[2] + pr[3]);
+        m_run = m_new;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+            o[n][0] *= corr;
+            o[n][1] *= corr;
+        }
+        // O += P V: P is the A operand (row g, positions 2t..2t+1 and 2t+8..+9).
+        const uint32_t pa[4] = {pack_bf16x2(pr[0], pr[1]), 0u, pack_bf16x2(pr[2], pr[3]), 0u};
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {  // dims 16jj .. 16jj+15 = n-tiles 2jj, 2jj+1
+            const int mtx = lane >> 3;
+            const int r = warp * 16 + (mtx & 1) * 8 + (lane & 7);
+            const int c = 16 * jj + 8 * (mtx >> 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_trans(vbase + (c >> 6) * BOX + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4), b0, b1, b2, b3);
+            mma_bf16_16816(o[2 * jj], pa, b0, b1, o[2 * jj]);
+            mma_bf16_16816(o[2 * jj + 1], pa, b2, b3, o[2 * jj + 1]);
+        }
+        fence_proxy_async_smem();  // ldmatrix reads before the stage's next TMA fill
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+    }
+    // The warp's row sums, then its record for the CTA merge.
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    constexpr int CT = CWARPS * 32;
+    named_bar_sync(1, CT);  // every warp is done with the ring
+    if (g < G) {
+        if (t == 0) {
+            red_m[warp * 8 + g] = m_run;
+            red_l[warp * 8 + g] = l_run;
+        }
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+            red_o[(warp * 8 + g) * HD + 8 * n + 2 * t] = o[n][0];
+            red_o[(warp * 8 + g) * HD + 8 * n + 2 * t + 1] = o[n][1];
         }
     }
-#pragma unroll
-    for (int h = 0; h < G; ++h) ps[h * CH + tid] = sc[h];
-    __syncthreads();
-    // Softmax statistics: warp w handles heads w, w+4, ...
-    for (int hh = warp; hh < G; hh += THREADS / 32) {
-        float v[CH / 32], mx = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < CH / 32; ++k) { v[k] = ps[hh * CH + lane + 32 * k]; mx = fmaxf(mx, v[k]); }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float sum = 0.0f;
-#pragma unroll
-        for (int k = 0; k < CH / 32; ++k) {
-            const float e = (v[k] == -INFINITY) ? 0.0f : __expf(v[k] - mx);
-            ps[hh * CH + lane + 32 * k] = e;
-            sum += e;
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) { stat[hh] = mx; stat[G + hh] = sum; }
-    }
-    __syncthreads();
-    // Unnormalised outputs: thread d accumulates o[h][d] over the chunk.
-    float o[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) o[h] = 0.0f;
-    {
-        const int d = tid, box = d >> 6, col = d & 63, chunk = col >> 3, within = (col & 7) * 2;
-        const char *vb = vs + box * BOX_BYTES;
-        for (int i = 0; i < len; ++i) {
-            float vv;
-            if (c0 + i == pos)
-                vv = vnew[d];
-            else
-                vv = bf16_bits_to_f32(*reinterpret_cast<const uint16_t *>(vb + i * 128 + ((chunk ^ (i & 7)) << 4) + within));
-#pragma unroll
-            for (int h = 0; h < G; ++h) o[h] = fmaf(ps[h * CH + i], vv, o[h]);
-        }
-    }
-    // Partial record of this chunk: m[G], l[G], o[G][HD].
-    const int pair = b * p.KVH + kvh;
-    float *rec = p.partial + (static_cast<int64_t>(pair) * p.max_chunks + c) * (G * (HD + 2));
-    if (tid < G) { rec[tid] = stat[tid]; rec[G + tid] = stat[G + tid]; }
-#pragma unroll
-    for (int h = 0; h < G; ++h) rec[2 * G + h * HD + tid] = o[h];
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) *flag = (atomicAdd(&p.counters[pair], 1u) == static_cast<unsigned>(n_chunks - 1)) ? 1 : 0;
-    __syncthreads();
-    if (!*flag) return;
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    // Merge the chunks in order.  Output column of this thread: d, or its
-    // slot in the 4-bit qmv pair order (within 8 columns: 0 4 1 5 2 6 3 7).
-    const int e8 = tid & 7;
-    const int out_col = p.out_pair_order ? (tid & ~7) + (e8 < 4 ? 2 * e8 : 2 * (e8 - 4) + 1) : tid;
-    const float *recs = p.partial + static_cast<int64_t>(pair) * p.max_chunks * (G * (HD + 2));
+    named_bar_sync(1, CT);
+    // CTA result for (head h, dim d): threads take d = tid, all G heads.
+    const int d = tid;
+    float cm[G], cl[G], co[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
         float M = -INFINITY;
-        for (int cc = 0; cc < n_chunks; ++cc) M = fmaxf(M, __ldcg(&recs[cc * (G * (HD + 2)) + h]));
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, red_m[w * 8 + h]);
         float L = 0.0f, O = 0.0f;
-        for (int cc = 0; cc < n_chunks; ++cc) {
-            const float *r = recs + cc * (G * (HD + 2));
-            const float w = __expf(__ldcg(&r[h]) - M);
-            L = fmaf(__ldcg(&r[G + h]), w, L);
-            O = fmaf(__ldcg(&r[2 * G + h * HD + tid]), w, O);
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) {
+            const float wt = M == -INFINITY ? 0.0f : exp2f(red_m[w * 8 + h] - M);
+            L = fmaf(red_l[w * 8 + h], wt, L);
+            O = fmaf(red_o[(w * 8 + h) * HD + d], wt, O);
         }
-        p.out[b * p.ld_out + (kvh * G + h) * HD + out_col] = f32_to_bf16_bits(O / L);
+        cm[h] = M;
+        cl[h] = L;
+        co[h] = O;
+    }
+    const int col = out_column(d, p.out_pair_order);
+    if (p.splits == 1) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) p.out[b * p.ld_out + (kvh * G + h) * HD + col] = f32_to_bf16_bits(co[h] / cl[h]);
+        return;
+    }
+    constexpr int REC = G * (HD + 2);
+    float *rec = p.partial + (static_cast<int64_t>(pair) * p.splits + split) * REC;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        rec[2 * G + h * HD + d] = co[h];
+        if (d == 0) {
+            rec[h] = cm[h];
+            rec[G + h] = cl[h];
+        }
+    }
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    named_bar_sync(1, CT);
+    if (tid == 0) *flag = (atomicAdd(&p.counters[pair], 1u) == static_cast<unsigned>(p.splits - 1)) ? 1 : 0;
+    named_bar_sync(1, CT);
+    if (!*flag) return;
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    // Last CTA of the pair: merge the splits in order (loads issued together).
+    const float *recs = p.partial + static_cast<int64_t>(pair) * p.splits * REC;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        float ms[MAX_SPLITS];
+#pragma unroll
+        for (int s2 = 0; s2 < MAX_SPLITS; ++s2) ms[s2] = s2 < p.splits ? __ldcg(recs + s2 * REC + h) : -INFINITY;
+        float M = -INFINITY;
+#pragma unroll
+        for (int s2 = 0; s2 < MAX_SPLITS; ++s2) M = fmaxf(M, ms[s2]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int s2 = 0; s2 < MAX_SPLITS; ++s2) {
+            if (s2 < p.splits) {
+                const float wt = ms[s2] == -INFINITY ? 0.0f : exp2f(ms[s2] - M);
+                L = fmaf(__ldcg(recs + s2 * REC + G + h), wt, L);
+                O = fmaf(__ldcg(recs + s2 * REC + 2 * G + h * HD + d), wt, O);
+            }
+        }
+        p.out[b * p.ld_out + (kvh * G + h) * HD + col] = f32_to_bf16_bits(O / L);
     }
     if (tid == 0) atomicExch(&p.counters[pair], 0u);
 }
 
 // h[b][:] = table[tokens[b]][:] (bf16 -> f32), the per-16-column sums of
-// squares of h for the first norm, and a cleared argmax buffer.
-__global__ void embed_kernel(const uint16_t *table, int64_t ld_table, const int *tokens, int B, int D, float *h,
-                             float *ss_out, unsigned long long *amax) {
+// squares of h for the first norm ([D/16][kSsWidth]), and a cleared argmax
+// buffer.  A token outside [0, vocab) reads row 0 instead and sets the status
+// word.
+__global__ void embed_kernel(const uint16_t *table, int64_t ld_table, int64_t vocab, const int *tokens, int B, int D,
+                             float *h, float *ss_out, unsigned long long *amax, unsigned *status) {
+    pdl_wait();
     const int b = blockIdx.y;
     const int tile = blockIdx.x * (blockDim.x / 16) + threadIdx.x / 16;  // 16 columns per tile
     const int col = tile * 16 + (threadIdx.x & 15);
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < B) amax[threadIdx.x] = 0ull;
+    int tok = tokens[b];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(status, static_cast<unsigned>(DEV_BOUNDS));
+        tok = 0;
+    }
     float v = 0.0f;
     if (col < D) {
-        v = bf16_bits_to_f32(table[static_cast<int64_t>(tokens[b]) * ld_table + col]);
+        v = bf16_bits_to_f32(table[static_cast<int64_t>(tok) * ld_table + col]);
         h[static_cast<int64_t>(b) * D + col] = v;
     }
     float sq = v * v;
 #pragma unroll
     for (int o = 8; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if ((threadIdx.x & 15) == 0 && col < D) ss_out[tile * 16 + b] = sq;
+    if ((threadIdx.x & 15) == 0 && col < D) ss_out[tile * kSsWidth + b] = sq;
 }
 
-// tokens[b] = argmax index from the packed maxima; history[step][b] keeps it;
-// the position advances by one.
-__global__ void finalize_kernel(const unsigned long long *amax, int B, int *tokens, int *history, int *pos,
-                                int *step) {
+// tokens[b] = argmax index from the packed maxima; history[step % rows][b]
+// keeps it (a ring of the last `rows` steps); the position advances by one.
+__global__ void finalize_kernel(const unsigned long long *amax, int B, int *tokens, int *history, int history_rows,
+                                int *pos, int *step) {
+    pdl_wait();
     const int b = threadIdx.x;
     const int s = *step;
     if (b < B) {
         const int tok = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(amax[b] & 0xFFFFFFFFull));
         tokens[b] = tok;
-        if (history) history[s * B + b] = tok;
+        if (history && history_rows > 0) history[(s % history_rows) * B + b] = tok;
     }
     __syncthreads();
     if (b == 0) {
@@ -253,7 +385,25 @@ __global__ void finalize_kernel(const unsigned long long *amax, int B, int *toke
 
 }  // namespace dec
 
-cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, cudaStream_t stream) {
+int attention_splits(int batch, int kv_heads, int capacity, int num_sms) {
+    // All CTAs resident at once (two per SM) in a single wave, each with at
+    // least two tiles of the longest context.
+    const int pairs = batch * kv_heads;
+    int s = 2 * num_sms / pairs;
+    const int tiles = (capacity + dec::TILE - 1) / dec::TILE;
+    s = s < tiles / 2 ? s : tiles / 2;
+    s = s < dec::MAX_SPLITS ? s : dec::MAX_SPLITS;
+    return s < 1 ? 1 : s;
+}
+
+size_t attention_workspace_bytes(int batch, int kv_heads, int q_heads, int capacity, int num_sms) {
+    const int G = q_heads / kv_heads;
+    return kPartialOffset + size_t(batch) * kv_heads * attention_splits(batch, kv_heads, capacity, num_sms) * G *
+                                (dec::HD + 2) * 4;
+}
+
+cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, int num_sms, cudaStream_t stream,
+                                    bool pdl) {
     if (a.head_dim != dec::HD || a.q_heads % a.kv_heads) return cudaErrorInvalidValue;
     const int G = a.q_heads / a.kv_heads;
     dec::AttnParams p{};
@@ -273,7 +423,7 @@ cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, cu
     p.QH = a.q_heads;
     p.KVH = a.kv_heads;
     p.cap = a.capacity;
-    p.max_chunks = (a.capacity + dec::CH - 1) / dec::CH;
+    p.splits = attention_splits(a.batch, a.kv_heads, a.capacity, num_sms);
     p.scale = a.scale;
     p.out_pair_order = a.out_pair_order;
     char *ws = static_cast<char *>(workspace);
@@ -282,46 +432,49 @@ cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, cu
     p.partial = reinterpret_cast<float *>(ws + kPartialOffset);
     const uint64_t rows = static_cast<uint64_t>(a.batch) * a.kv_heads * a.capacity;
     const CUtensorMap *km = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.k_cache, dec::HD, rows,
-                                                 dec::HD * 2, 64, dec::CH, CU_TENSOR_MAP_SWIZZLE_128B);
+                                                 dec::HD * 2, 64, dec::TILE, CU_TENSOR_MAP_SWIZZLE_128B);
     const CUtensorMap *vm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.v_cache, dec::HD, rows,
-                                                 dec::HD * 2, 64, dec::CH, CU_TENSOR_MAP_SWIZZLE_128B);
+                                                 dec::HD * 2, 64, dec::TILE, CU_TENSOR_MAP_SWIZZLE_128B);
     if (!km || !vm) return cudaErrorInvalidValue;
-    const int smem = 1024 + 4 * dec::BOX_BYTES + (G * dec::HD + G * dec::CH + 2 * dec::HD + 2 * G + 2) * 4 + 64;
-    dim3 grid(p.max_chunks, a.kv_heads, a.batch);
+    const int smem = 1024 + dec::STAGES * dec::STAGE_BYTES + 2 * dec::STAGES * 8 + 16;
+    dim3 grid(p.splits, a.kv_heads, a.batch);
     cudaError_t e;
     switch (G) {
     case 4:
         if ((e = ensure_smem_attr(reinterpret_cast<const void *>(dec::decode_attention_kernel<4>), smem)) != cudaSuccess)
             return e;
-        dec::decode_attention_kernel<4><<<grid, dec::THREADS, smem, stream>>>(*km, *vm, p);
+        e = launch_ex(dec::decode_attention_kernel<4>, grid, dim3(dec::THREADS), smem, stream, false, pdl, *km, *vm, p);
         break;
     case 8:
         if ((e = ensure_smem_attr(reinterpret_cast<const void *>(dec::decode_attention_kernel<8>), smem)) != cudaSuccess)
             return e;
-        dec::decode_attention_kernel<8><<<grid, dec::THREADS, smem, stream>>>(*km, *vm, p);
+        e = launch_ex(dec::decode_attention_kernel<8>, grid, dim3(dec::THREADS), smem, stream, false, pdl, *km, *vm, p);
         break;
     default:
         return cudaErrorInvalidValue;
     }
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
-cudaError_t launch_embed(const void *table, int64_t ld_table, const int *tokens, int B, int D, float *h, float *ss_out,
-                         unsigned long long *amax, cudaStream_t stream) {
+cudaError_t launch_embed(const void *table, int64_t ld_table, int64_t vocab, const int *tokens, int B, int D,
+                         float *h, float *ss_out, unsigned long long *amax, void *workspace, cudaStream_t stream,
+                         bool pdl) {
     const int threads = 256;  // 16 tiles of 16 columns per block
     dim3 grid((D + threads - 1) / threads, B);
-    dec::embed_kernel<<<grid, threads, 0, stream>>>(static_cast<const uint16_t *>(table), ld_table, tokens, B, D, h,
-                                                   ss_out, amax);
+    cudaError_t e = launch_ex(dec::embed_kernel, grid, dim3(threads), 0, stream, false, pdl,
+                              static_cast<const uint16_t *>(table), ld_table, vocab, tokens, B, D, h, ss_out, amax,
+                              static_cast<unsigned *>(workspace));
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
-cudaError_t launch_finalize(const unsigned long long *amax, int B, int *tokens, int *history, int *pos, int *step,
-                            cudaStream_t stream) {
-    dec::finalize_kernel<<<1, 32 * ((B + 31) / 32), 0, stream>>>(amax, B, tokens, history, pos, step);
+cudaError_t launch_finalize(const unsigned long long *amax, int B, int *tokens, int *history, int history_rows,
+                            int *pos, int *step, cudaStream_t stream, bool pdl) {
+    cudaError_t e = launch_ex(dec::finalize_kernel, dim3(1), dim3(32 * ((B + 31) / 32)), 0, stream, false, pdl, amax,
+                              B, tokens, history, history_rows, pos, step);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 }  // namespace afb

@@ -26,7 +26,7 @@ struct QmmArgs {
 // output element, same operation order as the CPU oracle.
 cudaError_t launch_qmm_generic(const QmmArgs &a, cudaStream_t stream);
 
-// Decode qmv for M <= 16, bits in {4, 8}, group 64, bf16 x/s/b, dense rows.
+// Decode qmv for M <= 32, bits in {4, 8}, group 64, bf16 x/s/b, dense rows.
 struct QmvPlan {
     int splits;      // K splits (>= 1; 0 = not plannable): x slices that fit shared memory
     int ks;          // K per split
@@ -34,6 +34,8 @@ struct QmvPlan {
     int stages;      // shared-memory ring depth
     int max_slots;   // partial-sum slots per block in the workspace
     int smem_bytes;
+    int variant;     // kernel instantiation (activation fragments, tiles per warp, consumer warps)
+    int rows;        // weight rows per block
 };
 
 // Context workspace layout: [0, 256) device status words (a bounded wait that
@@ -41,6 +43,11 @@ struct QmvPlan {
 // counters (first half) and completion counters (second half), zero between
 // launches; [kPartialOffset, ...) f32 partial sums.
 constexpr size_t kCounterOffset = 256;
+// Most activation rows the decode qmv takes in one pass, and the row width of
+// the per-16-column sums of squares ([cols/16][kSsWidth] f32) that the
+// residual epilogue writes and the RMSNorm prologue reads.
+constexpr int kMaxQmvRows = 32;
+constexpr int kSsWidth = 32;
 constexpr int64_t kMaxTiles = 262144;
 constexpr size_t kPartialOffset = kCounterOffset + size_t(kMaxTiles) * 4;
 // Optional fusions of the decode qmv (decoder use).  Activations: natural
@@ -63,6 +70,7 @@ struct QmvFusion {
     int64_t ld_act = 0;
     int act_pair_order = 0;         // EPI_SILU_MUL: write act in the 4-bit pair order
     unsigned long long *amax = nullptr;  // EPI_ARGMAX: [M]
+    int64_t index_offset = 0;       // EPI_ARGMAX: added to the row index (a vocabulary shard's first row)
 };
 bool qmv_supported(const QmmArgs &a, const char **why);
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes);
@@ -75,9 +83,20 @@ size_t qmv_prep_bytes(const QmmArgs &a);
 // the per-16-column partial sums of squares ss ([ss_tiles][16]) and gamma.
 cudaError_t launch_qmv_prep(const void *src, int64_t ld_src, int mode, const float *ss, int ss_tiles,
                             const uint16_t *gamma, float eps, int M, int K, int bits, uint16_t *dst, int64_t ld_dst,
-                            cudaStream_t stream);
+                            cudaStream_t stream, bool pdl = false);
+// pdl: launch with programmatic dependent launch (the kernel prefetches its
+// weights before waiting for the preceding kernel in the stream).
 cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &p, void *workspace, cudaStream_t stream,
-                       const QmvFusion *fusion = nullptr);
+                       const QmvFusion *fusion = nullptr, bool pdl = false);
+// h[m] += add[m] (add may be null), then dst[m] = bf16(rmsnorm(h[m]) * gamma)
+// in the qmv's column order for `bits`; one CTA per row, K <= 8192.
+cudaError_t launch_resid_norm(float *h, int64_t ld_h, const float *add, int64_t ld_add, const uint16_t *gamma,
+                              float eps, int M, int K, int bits, uint16_t *dst, int64_t ld_dst, cudaStream_t stream,
+                              bool pdl);
+// Test hook of the split-K combine: its wait limit (0 = the default) and
+// arrivals it waits for beyond the real contributors (0 in normal use; 1
+// makes every shared block's wait run out).  Process-wide.
+void qmv_set_combine_wait(uint64_t limit_ns, unsigned extra_arrivals);
 
 // Decoder kernels around the quantized linears (decode.cu).
 struct DecodeAttnArgs {
@@ -93,11 +112,17 @@ struct DecodeAttnArgs {
     float scale;
     int out_pair_order;             // write out in the 4-bit qmv pair order
 };
-cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, cudaStream_t stream);
-cudaError_t launch_embed(const void *table, int64_t ld_table, const int *tokens, int B, int D, float *h, float *ss_out,
-                         unsigned long long *amax, cudaStream_t stream);
-cudaError_t launch_finalize(const unsigned long long *amax, int B, int *tokens, int *history, int *pos, int *step,
-                            cudaStream_t stream);
+// Context splits per (batch row, KV head) and the workspace the attention's
+// split records need (f32, after kPartialOffset).
+int attention_splits(int batch, int kv_heads, int capacity, int num_sms);
+size_t attention_workspace_bytes(int batch, int kv_heads, int q_heads, int capacity, int num_sms);
+cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, int num_sms, cudaStream_t stream,
+                                    bool pdl);
+cudaError_t launch_embed(const void *table, int64_t ld_table, int64_t vocab, const int *tokens, int B, int D,
+                         float *h, float *ss_out, unsigned long long *amax, void *workspace, cudaStream_t stream,
+                         bool pdl);
+cudaError_t launch_finalize(const unsigned long long *amax, int B, int *tokens, int *history, int history_rows,
+                            int *pos, int *step, cudaStream_t stream, bool pdl);
 
 // Prefill qmm on tcgen05 tensor cores (M >= 64), bf16 x/s/b, 4/8-bit, group 64.
 bool qmm_tc_supported(const QmmArgs &a, const char **why);
@@ -108,7 +133,29 @@ void count_launch(uint64_t n = 1);
 }  // namespace afb
 
 struct affon_b200_qmm_desc;
+
 namespace afb {
+struct TpState;
+}
+
+// A context: one device, one stream, a workspace, and (after
+// affon_b200_tp_init) its place in a tensor-parallel group.
+struct affon_b200_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    bool overlap = false;  // programmatic dependent launch for the decode kernels
+    void *workspace = nullptr;
+    size_t workspace_bytes = 0;
+    // Staging buffers of the host-buffer entry points (grown on demand).
+    void *stage[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t stage_bytes[5] = {0, 0, 0, 0, 0};
+    afb::TpState *tp = nullptr;
+};
+
+namespace afb {
+// Tears down the context's tensor-parallel state (tp.cu).
+void tp_release(affon_b200_ctx *ctx);
 // Descriptor validation, argument resolution and the thread-local error
 // message of the C ABI (abi.cu), for other entry points of the library.
 int validate_qmm_desc(const affon_b200_qmm_desc *d);

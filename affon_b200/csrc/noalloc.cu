@@ -2,14 +2,14 @@
 //
 // Some callers cannot let a library allocate device memory: a runtime that
 // reserves every byte of the GPU in its own arena at start-up and forbids
-// allocations behind its back, a plugin host whose allocator is the only one
-// allowed to call into the driver, or code that is running while a stream is
-// being captured, where cudaMalloc is not permitted.  The regular entry
-// points need an affon_b200 context, and creating one allocates the split-K
-// workspace.  affon_b200_qmv_noalloc() instead keeps the decode qmv's scratch
-// (status word, per-block arrival counters and partial sums) in the static
-// device array below, which every GPU that loads this library holds until
-// the process exits.
+// allocations behind its back, or a plugin host whose allocator is the only
+// one allowed to call into the driver.  The regular entry points need an
+// affon_b200 context, and creating one allocates the split-K workspace.
+// affon_b200_qmv_noalloc() instead keeps the decode qmv's scratch (status
+// word, per-block arrival counters and partial sums) in the static device
+// array below, which every GPU that loads this library holds until the
+// process exits.  affon_b200_qmv_noalloc_status() reads that array's status
+// word back, so such a caller can still learn that a bounded wait gave up.
 //
 // The array's name in host code is only a host-side stand-in for the
 // symbol, never a device address; the device address is looked up once per
@@ -83,5 +83,22 @@ extern "C" int affon_b200_qmv_noalloc(const affon_b200_qmm_desc *desc, const voi
                              0, counters, stream)) != cudaSuccess)
         return afb::set_cuda_error(e, "cudaMemsetAsync(qmv scratch)");
     if ((e = afb::launch_qmv(a, plan, scratch, stream)) != cudaSuccess) return afb::set_cuda_error(e, "qmv launch");
+    return AFFON_B200_OK;
+}
+
+extern "C" int affon_b200_qmv_noalloc_status(void *cuda_stream, uint32_t *status_out) {
+    afb::clear_error();
+    if (!status_out) return afb::set_error(AFFON_B200_INVALID_ARG, "qmv_noalloc_status: null output");
+    *status_out = 0;
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(cuda_stream));
+    if (e != cudaSuccess)
+        return afb::set_cuda_error(e, "stream synchronize");
+    // The status word is the array's first 4 bytes (kCounterOffset layout).
+    unsigned status = 0;
+    if ((e = cudaMemcpyFromSymbol(&status, g_qmv_scratch, sizeof status, 0, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return afb::set_cuda_error(e, "cudaMemcpyFromSymbol(qmv scratch status)");
+    *status_out = status;
+    if (status != 0)
+        return afb::set_error(AFFON_B200_TIMEOUT, "qmv_noalloc: a bounded wait gave up; the last result is invalid");
     return AFFON_B200_OK;
 }

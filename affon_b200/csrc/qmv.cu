@@ -1,17 +1,29 @@
-// Decode qmv for sm_100a: y[M,N] = x[M,K] . decode(W)[N,K]^T for M <= 16,
+// Decode qmv for sm_100a: y[M,N] = x[M,K] . decode(W)[N,K]^T for M <= 32,
 // 4- or 8-bit codes packed little-endian into u32 along K, group 64, bf16
 // activations / scales / biases, f32 accumulation (the layout and formula of
 // docs/core/quantized-inference.md:45-67).
 //
 // Streaming.  Persistent CTAs, one per SM.  One producer warp moves each
-// 384-row x 128-byte stage of the packed weight matrix through a ring of
+// block-row x 128-byte stage of the packed weight matrix through a ring of
 // shared-memory stages with 2D TMA loads (128-byte swizzle), together with the
-// matching 384 x 8 boxes of bf16 scales and biases and the stage's activation
-// columns (16 rows x 64 columns per group, 128-byte swizzle).  The ring holds
-// ~190 KB per SM in flight without costing registers, and the activations
-// need no separate staging pass.  Twelve consumer warps (two 16-row weight
-// tiles each, so each activation fragment feeds two tiles) decode the packed
-// words in registers and feed tensor cores.
+// matching boxes of bf16 scales and biases (8 groups wide) and the stage's
+// activation columns (16 or 32 rows x 64 columns per group, 128-byte swizzle).
+// The ring holds ~190 KB per SM in flight without costing registers, and the
+// activations need no separate staging pass.  Twelve consumer warps decode the
+// packed words in registers and feed tensor cores: for M <= 16 each warp owns
+// two 16-row weight tiles (384-row blocks), so each activation fragment feeds
+// two tiles; for 16 < M <= 32 one tile (192-row blocks) with four 8-row
+// activation fragments.
+//
+// Overlap with the preceding kernel.  With programmatic dependent launch
+// (the context's overlap mode) a CTA may start while the kernel before it in
+// the stream is still finishing: the producer fills the first ring stages
+// with weights, scales and biases -- which no preceding kernel writes in that
+// mode -- and only then waits for the preceding kernel (griddepcontrol.wait)
+// before loading activations; every other warp waits before touching any
+// global memory.  Each CTA also lets the following kernel launch as soon as it
+// starts; the following kernel can then only take SMs this grid leaves idle or
+// has finished with, and all CTAs of this grid are already resident.
 //
 // Why mma.sync tensor cores at M <= 16: at ~6.5 TB/s a 4-bit weight stream
 // delivers ~13e12 weights/s; decoding each weight to a float and multiplying
@@ -51,6 +63,7 @@
 // the epilogue; results do not depend on scheduling.  The last CTA to finish
 // a block resets its counters for the next launch.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 #include "common.cuh"
@@ -62,23 +75,37 @@ namespace qmv {
 
 constexpr int GROUP = 64;
 constexpr int MAX_STAGES = 8;
-constexpr int X_BOX_BYTES = 16 * 128;  // one group of activation columns: 16 rows x 64 bf16
-constexpr int CONSUMERS = 12;          // consumer warps: two 16-row weight tiles each, 384-row blocks
-constexpr int NT = 2;                  // 16-row weight tiles per consumer warp
-constexpr int ROWS = 16 * NT * CONSUMERS;
-constexpr int BOX_ROWS = 128;          // TMA box height for weights, scales and biases
-static_assert(ROWS % BOX_ROWS == 0, "block rows");
-constexpr int THREADS = 32 * (CONSUMERS + 2);  // consumers, producer, sum warp
+constexpr int MAX_XR = 32;             // activation rows staged per group, at most
 
-template <int BITS>
+// Consumer warps (CW), 16-row weight tiles per consumer warp (NT) and 8-row
+// activation fragments (MT) of one instantiation; a block is the CTA-wide
+// row tile (CW * NT * 16 rows), loaded as NT TMA boxes of CW * 16 rows.
+// The register file of each of the SM's four sub-partitions (16K registers)
+// holds a quarter of the CTA's warps, rounded up: 14 warps (12 consumers)
+// allow 128 registers per thread, 12 warps (10 consumers) 168, which the
+// M > 8 variants need to keep their accumulators out of local memory.
+template <int BITS, int MT, int NT, int CW>
 struct Shape {
-    static constexpr int GPS = BITS == 4 ? 4 : 2;  // groups per stage (128 packed bytes per row)
-    static constexpr int KPS = GPS * GROUP;         // K per stage
-    static constexpr int W = ROWS * 128;            // packed bytes per stage
-    static constexpr int SB = ROWS * 16;            // one 8-group box of scales (or biases)
-    static constexpr int X = GPS * X_BOX_BYTES;
-    static constexpr int BYTES = W + 2 * SB + X;    // all offsets stay 1024-byte aligned
+    static constexpr int THREADS = 32 * (CW + 2);     // consumers, producer, sum warp
+    static constexpr int ROWS = 16 * NT * CW;         // weight rows per block
+    static constexpr int BOX_ROWS = 16 * CW;          // TMA box height for weights, scales and biases
+    static constexpr int XR = MT == 4 ? 32 : 16;      // activation rows per staged box
+    static constexpr int X_BOX = XR * 128;            // one group of activation columns: XR rows x 64 bf16
+    static constexpr int GPS = BITS == 4 ? 4 : 2;     // groups per stage (128 packed bytes per row)
+    static constexpr int KPS = GPS * GROUP;           // K per stage
+    static constexpr int W = ROWS * 128;              // packed bytes per stage
+    static constexpr int SB = ROWS * 16;              // one 8-group box of scales (or biases)
+    static constexpr int X = GPS * X_BOX;
+    static constexpr int BYTES = W + 2 * SB + X;      // swizzled regions (W, X) stay 1024-byte aligned
+    static_assert(W % 1024 == 0 && (2 * SB) % 1024 == 0 && X % 1024 == 0 && BOX_ROWS <= 256, "stage layout");
 };
+
+// Instantiations (variant: MT, NT, CW -> block rows): M <= 8: 0 = (1, 2, 12)
+// -> 384, 1 = (1, 1, 12) -> 192; M <= 16: 2 = (2, 2, 10) -> 320, 3 = (2, 1, 10)
+// -> 160; M <= 32: 4 = (4, 1, 10) -> 160.  The planner picks, per shape, the
+// variant with the smallest estimated makespan.
+constexpr int kVariantRows[5] = {384, 192, 320, 160, 160};
+constexpr int kVariantNT[5] = {2, 1, 2, 1, 1};
 
 struct Params {
     void *y;
@@ -92,6 +119,8 @@ struct Params {
     int stages;           // ring depth
     int max_slots;        // partial slots per block
     int y_bf16;
+    uint64_t arrival_wait_ns;  // limit of the combine's wait for the other contributors
+    unsigned extra_arrivals;   // test hook: contributors the combine waits for beyond the real ones (0)
     QmvFusion f;
 };
 
@@ -164,14 +193,17 @@ __device__ __forceinline__ unsigned long long epilogue_pair(const Params &p, int
             p.f.act[m * p.f.ld_act + j] = f32_to_bf16_bits(silu * v_hi);
         }
         break;
-    case EPI_ARGMAX:
-        if (ok_lo) best = (static_cast<unsigned long long>(f32_order_key(v_lo)) << 32) | (0xFFFFFFFFu - uint32_t(n_lo));
+    case EPI_ARGMAX: {
+        const int64_t off = p.f.index_offset;
+        if (ok_lo)
+            best = (static_cast<unsigned long long>(f32_order_key(v_lo)) << 32) | (0xFFFFFFFFu - uint32_t(n_lo + off));
         if (ok_hi) {
             const unsigned long long c =
-                (static_cast<unsigned long long>(f32_order_key(v_hi)) << 32) | (0xFFFFFFFFu - uint32_t(n_hi));
+                (static_cast<unsigned long long>(f32_order_key(v_hi)) << 32) | (0xFFFFFFFFu - uint32_t(n_hi + off));
             best = c > best ? c : best;
         }
         break;
+    }
     default:
         if (ok_lo) store_out(p, m, n_lo, v_lo);
         if (ok_hi) store_out(p, m, n_hi, v_hi);
@@ -188,7 +220,7 @@ __device__ __forceinline__ void publish_tile(const Params &p, int64_t tile, int 
         ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
         ssq += __shfl_xor_sync(0xffffffffu, ssq, 8);
         ssq += __shfl_xor_sync(0xffffffffu, ssq, 16);
-        if (lead && m < p.M) p.f.ss_out[tile * 16 + m] = ssq;
+        if (lead && m < p.M) p.f.ss_out[tile * kSsWidth + m] = ssq;
     } else if (p.f.epi == EPI_ARGMAX) {
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) {
@@ -234,7 +266,7 @@ __device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, fl
         ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
         ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
         ssq += __shfl_xor_sync(0xffffffffu, ssq, 8);
-        if (ok && (lane & 15) == 0) p.f.ss_out[(n >> 4) * 16 + m] = ssq;
+        if (ok && (lane & 15) == 0) p.f.ss_out[(n >> 4) * kSsWidth + m] = ssq;
         break;
     }
     case EPI_SILU_MUL: {
@@ -249,7 +281,8 @@ __device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, fl
     }
     case EPI_ARGMAX: {
         unsigned long long best =
-            ok ? (static_cast<unsigned long long>(f32_order_key(v)) << 32) | (0xFFFFFFFFu - uint32_t(n)) : 0ull;
+            ok ? (static_cast<unsigned long long>(f32_order_key(v)) << 32) | (0xFFFFFFFFu - uint32_t(n + p.f.index_offset))
+               : 0ull;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
@@ -275,10 +308,11 @@ __device__ __forceinline__ void block_contributors(const Params &p, int blk, int
 // writes its f32 partial slot and announces it on the block's arrival
 // counter; the sums are formed in combine_blocks once every contributor has
 // written its slot.
-template <int MT>
+template <int MT, int NT, int CW>
 __device__ __forceinline__ void segment_epilogue(const Params &p, const float (&acc)[NT][MT][4], int blk, int warp,
                                                  int g, int t, int tid) {
-    constexpr int CT = CONSUMERS * 32;  // consumer threads
+    constexpr int CT = CW * 32;  // consumer threads
+    constexpr int ROWS = 16 * NT * CW;
     int first, total;
     block_contributors(p, blk, first, total);
     const int64_t nb0 = static_cast<int64_t>(blk) * ROWS;
@@ -313,16 +347,17 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *a) {
     return v;
 }
 
-// Second phase (the launch is cooperative, so every CTA of the grid is
-// resident): for each block this CTA contributed to, wait until all its
-// contributors have published their slots, then sum the slots in slot order
-// for this CTA's share of the block's 16-row tiles and apply the epilogue.
-// The CTA finishing last resets the block's counters for the next launch.
-// The wait is bounded; on timeout the status word says TIMEOUT.
-template <int MT>
+// Second phase (every CTA of the grid is resident): for each block this CTA
+// contributed to, wait until all its contributors have published their
+// slots, then sum the slots in slot order for this CTA's share of the
+// block's 16-row tiles and apply the epilogue.  The CTA finishing last resets
+// the block's counters for the next launch.  The wait is bounded; on timeout
+// the status word says TIMEOUT and the CTA goes on (its results are then
+// garbage, and the counters are still reset).
+template <int ROWS, int CW>
 __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp, int lane, int tid,
                                volatile int *abort) {
-    constexpr int CT = CONSUMERS * 32, TILES = ROWS / 16, BATCH = 8;
+    constexpr int CT = CW * 32, TILES = ROWS / 16, BATCH = 8;
     if (hi <= lo) return;
     unsigned *done = p.counters + kMaxTiles / 2;
     const int b_first = static_cast<int>(lo / p.spb), b_last = static_cast<int>((hi - 1) / p.spb);
@@ -332,9 +367,10 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
         if (total == 1) continue;
         const int slot = static_cast<int>(blockIdx.x) - first;
         if (tid == 0) {
+            const unsigned want = static_cast<unsigned>(total) + p.extra_arrivals;
             const uint64_t start = globaltimer();
-            while (ld_acquire_gpu(&p.counters[blk]) < static_cast<unsigned>(total)) {
-                if (*abort || globaltimer() - start > 2000000000ull) {
+            while (ld_acquire_gpu(&p.counters[blk]) < want) {
+                if (*abort || globaltimer() - start > p.arrival_wait_ns) {
                     *abort = 1;
                     atomicExch(p.status, static_cast<unsigned>(DEV_TIMEOUT));
                     break;
@@ -349,7 +385,7 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
         const int row0 = t0 * 16, nrows = (t1 - t0) * 16;
         const int chunks = (nrows + 31) / 32;
         // Work unit = (32-row chunk, activation row m), one warp each.
-        for (int u = warp; u < chunks * p.M; u += CONSUMERS) {
+        for (int u = warp; u < chunks * p.M; u += CW) {
             const int chunk = u / p.M, m = u - chunk * p.M;
             const int rr = chunk * 32 + lane;
             const bool active = rr < nrows;
@@ -374,23 +410,25 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
     }
 }
 
-template <int BITS, int MT>
-__global__ void __launch_bounds__(THREADS, 1)
+template <int BITS, int MT, int NT, int CW>
+__global__ void __launch_bounds__(32 * (CW + 2), 1)
     qmv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap xmap, Params p) {
-    using Sh = Shape<BITS>;
-    constexpr int GPS = Sh::GPS, KPS = Sh::KPS, CW = CONSUMERS;
+    using Sh = Shape<BITS, MT, NT, CW>;
+    constexpr int GPS = Sh::GPS, KPS = Sh::KPS, ROWS = Sh::ROWS, BOX_ROWS = Sh::BOX_ROWS;
     extern __shared__ char smem_raw[];
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
     char *ring = smem;
-    float *xsums = reinterpret_cast<float *>(ring + S * Sh::BYTES);  // [stage][group][16]
-    uint64_t *full = reinterpret_cast<uint64_t *>(xsums + MAX_STAGES * GPS * 16);
+    float *xsums = reinterpret_cast<float *>(ring + S * Sh::BYTES);  // [stage][group][XR]
+    uint64_t *full = reinterpret_cast<uint64_t *>(xsums + MAX_STAGES * GPS * MAX_XR);
     uint64_t *empty = full + MAX_STAGES;
     uint64_t *xsfull = empty + MAX_STAGES;
     volatile int *abort = reinterpret_cast<volatile int *>(xsfull + MAX_STAGES);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // The next kernel may launch once every CTA of this grid has started.
+    pdl_launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -413,13 +451,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_prefetch_desc(&smap);
             tma_prefetch_desc(&bmap);
             tma_prefetch_desc(&xmap);
-            int stage = 0;
-            uint32_t phase = 0, issued_mask = 0, issued_par = 0;
-            for (int64_t i = lo; i < hi; ++i) {
+            auto load_params = [&](int stage, int64_t i) {
                 const int blk = static_cast<int>(i / p.spb), st = static_cast<int>(i - int64_t(blk) * p.spb);
-                // On a timed-out wait (abort set) stop issuing loads; the other
-                // roles walk to the end without waiting.
-                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) break;
                 char *dst = ring + stage * Sh::BYTES;
                 mbar_arrive_expect_tx(&full[stage], Sh::BYTES);
                 const int kk = st * KPS;
@@ -431,9 +464,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tma_load_2d(dst + Sh::W + bx * BOX_ROWS * 16, &smap, &full[stage], g8, row0);
                     tma_load_2d(dst + Sh::W + Sh::SB + bx * BOX_ROWS * 16, &bmap, &full[stage], g8, row0);
                 }
+            };
+            auto load_x = [&](int stage, int64_t i) {
+                const int blk = static_cast<int>(i / p.spb), st = static_cast<int>(i - int64_t(blk) * p.spb);
+                char *dst = ring + stage * Sh::BYTES + Sh::W + 2 * Sh::SB;
 #pragma unroll
-                for (int G = 0; G < GPS; ++G)
-                    tma_load_2d(dst + Sh::W + 2 * Sh::SB + G * X_BOX_BYTES, &xmap, &full[stage], kk + G * GROUP, 0);
+                for (int G = 0; G < GPS; ++G) tma_load_2d(dst + G * Sh::X_BOX, &xmap, &full[stage], st * KPS + G * GROUP, 0);
+            };
+            // First pass over the ring: weights, scales and biases need nothing
+            // from the preceding kernel; the activations do.
+            const int pre = static_cast<int>(min(hi - lo, static_cast<int64_t>(S)));
+            for (int j = 0; j < pre; ++j) load_params(j, lo + j);
+            pdl_wait();
+            for (int j = 0; j < pre; ++j) load_x(j, lo + j);
+            int stage = pre % S;
+            uint32_t phase = pre == S ? 1u : 0u;
+            uint32_t issued_mask = (1u << pre) - 1u, issued_par = 0;  // stages 0..pre-1 at parity 0
+            for (int64_t i = lo + pre; i < hi; ++i) {
+                // On a timed-out wait (abort set) stop issuing loads; the other
+                // roles walk to the end without waiting.
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) break;
+                load_params(stage, i);
+                load_x(stage, i);
                 issued_mask |= 1u << stage;
                 issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
                 if (++stage == S) { stage = 0; phase ^= 1; }
@@ -444,6 +496,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         __syncwarp();
     } else if (warp == CW + 1) {  // ----------------------------- group sums
+        pdl_wait();
         // X_g = sum_{k in g} x[m][k] for every activation row, once per CTA and
         // stage, via m16n8k16 MMAs with an all-ones A operand (rows equal).
         const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 1.0 pairs
@@ -452,12 +505,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int64_t i = lo; i < hi; ++i) {
             mbar_wait(&full[stage], phase, abort, p.status);
             const char *xsb = ring + stage * Sh::BYTES + Sh::W + 2 * Sh::SB;
-            float *xs = xsums + stage * GPS * 16;
+            float *xs = xsums + stage * GPS * MAX_XR;
 #pragma unroll
             for (int G = 0; G < GPS; ++G)
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
-                    const char *row = xsb + G * X_BOX_BYTES + (g + 8 * mt) * 128;
+                    const char *row = xsb + G * Sh::X_BOX + (g + 8 * mt) * 128;
                     const uint4 v0 = *reinterpret_cast<const uint4 *>(row + (((2 * t) ^ g) << 4));
                     const uint4 v1 = *reinterpret_cast<const uint4 *>(row + (((2 * t + 1) ^ g) << 4));
                     float cx[4] = {0.f, 0.f, 0.f, 0.f};
@@ -466,8 +519,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mma_bf16_16816(cx, ones, v1.x, v1.y, cx);
                     mma_bf16_16816(cx, ones, v1.z, v1.w, cx);
                     if (g == 0) {  // cx[0], cx[1] = X of activation rows 2t, 2t+1 (+8 mt)
-                        xs[G * 16 + 8 * mt + 2 * t] = cx[0];
-                        xs[G * 16 + 8 * mt + 2 * t + 1] = cx[1];
+                        xs[G * MAX_XR + 8 * mt + 2 * t] = cx[0];
+                        xs[G * MAX_XR + 8 * mt + 2 * t + 1] = cx[1];
                     }
                 }
             fence_proxy_async_smem();  // x reads before the stage's next TMA fill
@@ -479,6 +532,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (++stage == S) { stage = 0; phase ^= 1; }
         }
     } else {  // ------------------------------------------------- consumers
+        pdl_wait();
         int stage = 0;
         uint32_t phase = 0;
         int64_t i = lo;
@@ -519,14 +573,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                 mbar_wait(&xsfull[stage], phase, abort, p.status);
-                const float *xs = xsums + stage * GPS * 16;
+                const float *xs = xsums + stage * GPS * MAX_XR;
 #pragma unroll
                 for (int G = 0; G < GPS; ++G) {
-                    // B fragments: row m = g + 8*mt of the group's 16 x 64 box,
+                    // B fragments: row m = g + 8*mt of the group's XR x 64 box,
                     // columns 16t..16t+15 = 16-byte chunks 2t, 2t+1 stored at
                     // chunk ^ (m % 8) (128-byte swizzle).
                     uint32_t xf[MT][8];
-                    const char *xb = xsb + G * X_BOX_BYTES;
+                    const char *xb = xsb + G * Sh::X_BOX;
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
                         const char *row = xb + (g + 8 * mt) * 128;
@@ -535,8 +589,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         xf[mt][0] = v0.x; xf[mt][1] = v0.y; xf[mt][2] = v0.z; xf[mt][3] = v0.w;
                         xf[mt][4] = v1.x; xf[mt][5] = v1.y; xf[mt][6] = v1.z; xf[mt][7] = v1.w;
                     }
-                    // A fragments of both tiles and all four k-steps first, then
-                    // the MMAs with tiles and m-tiles interleaved (NT * MT
+                    // A fragments of the warp's tiles and all four k-steps first,
+                    // then the MMAs with tiles and m-tiles interleaved (NT * MT
                     // independent accumulator chains).
                     uint32_t a[NT][4][4];
 #pragma unroll
@@ -588,7 +642,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     uint64_t xsum[MT];
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt)
-                        xsum[mt] = *reinterpret_cast<const uint64_t *>(xs + G * 16 + 8 * mt + 2 * t);
+                        xsum[mt] = *reinterpret_cast<const uint64_t *>(xs + G * MAX_XR + 8 * mt + 2 * t);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
                         const uint32_t s_w0 = sv[nt][0][G >> 1], s_w1 = sv[nt][1][G >> 1];
@@ -629,9 +683,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     accf[nt][mt][2] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][1]));
                     accf[nt][mt][3] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][1] >> 32));
                 }
-            segment_epilogue<MT>(p, accf, blk, warp, g, t, tid);
+            segment_epilogue<MT, NT, CW>(p, accf, blk, warp, g, t, tid);
         }
-        combine_blocks<MT>(p, lo, hi, warp, lane, tid, abort);
+        combine_blocks<ROWS, CW>(p, lo, hi, warp, lane, tid, abort);
     }
 }
 
@@ -642,13 +696,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 __global__ void prep_kernel(const void *src, int64_t ld_src, int mode, const float *ss, int ss_tiles,
                             const uint16_t *gamma, float eps, int M, int K, int pair_order, uint16_t *dst,
                             int64_t ld_dst) {
-    __shared__ float rms[16];
+    __shared__ float rms[kMaxQmvRows];
+    pdl_wait();
     if (mode == 1) {
         // 1/rms per row: one warp per row, fixed summation order.
         const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
         for (int m = w; m < M; m += blockDim.x / 32) {
             float sum = 0.0f;
-            for (int tl = lane; tl < ss_tiles; tl += 32) sum += ss[tl * 16 + m];
+            for (int tl = lane; tl < ss_tiles; tl += 32) sum += ss[tl * kSsWidth + m];
 #pragma unroll
             for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
             if (lane == 0) rms[m] = rsqrtf(sum / static_cast<float>(K) + eps);
@@ -691,15 +746,108 @@ __global__ void prep_kernel(const void *src, int64_t ld_src, int mode, const flo
     }
 }
 
+// Residual add and RMSNorm for the tensor-parallel decoder: one CTA per
+// activation row m.  h[m] += add[m] (when add is given; f32, in place), then
+// dst[m] = bf16(h[m] * rsqrt(mean(h[m]^2) + eps) * gamma) in the qmv's column
+// order.  The sum of squares is formed in a fixed order (per-thread partial
+// sums over a fixed column assignment, then a fixed tree), so every rank that
+// holds the same h computes the same bits.
+template <int PER>
+__global__ void __launch_bounds__(256) resid_norm_kernel(float *h, int64_t ld_h, const float *add, int64_t ld_add,
+                                                         const uint16_t *gamma, float eps, int K, int pair_order,
+                                                         uint16_t *dst, int64_t ld_dst) {
+    __shared__ float red[8];
+    pdl_wait();
+    const int m = blockIdx.x, tid = threadIdx.x;
+    float *hr = h + static_cast<int64_t>(m) * ld_h;
+    const float *ar = add ? add + static_cast<int64_t>(m) * ld_add : nullptr;
+    float v[PER * 8];
+    float ssq = 0.0f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int k0 = (j * 256 + tid) * 8;
+        if (k0 < K) {
+            float4 a0 = *reinterpret_cast<const float4 *>(hr + k0), a1 = *reinterpret_cast<const float4 *>(hr + k0 + 4);
+            if (ar) {
+                const float4 b0 = *reinterpret_cast<const float4 *>(ar + k0);
+                const float4 b1 = *reinterpret_cast<const float4 *>(ar + k0 + 4);
+                a0.x += b0.x; a0.y += b0.y; a0.z += b0.z; a0.w += b0.w;
+                a1.x += b1.x; a1.y += b1.y; a1.z += b1.z; a1.w += b1.w;
+                *reinterpret_cast<float4 *>(hr + k0) = a0;
+                *reinterpret_cast<float4 *>(hr + k0 + 4) = a1;
+            }
+            const float e[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[j * 8 + i] = e[i];
+                ssq = fmaf(e[i], e[i], ssq);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ssq;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += red[w];
+    const float r = rsqrtf(tot / static_cast<float>(K) + eps);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int k0 = (j * 256 + tid) * 8;
+        if (k0 < K) {
+            const uint4 gm = *reinterpret_cast<const uint4 *>(gamma + k0);
+            const uint32_t gw[4] = {gm.x, gm.y, gm.z, gm.w};
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t lo = f32_to_bf16_bits(v[j * 8 + 2 * e] * r * __uint_as_float(gw[e] << 16));
+                const uint32_t hi = f32_to_bf16_bits(v[j * 8 + 2 * e + 1] * r * __uint_as_float(gw[e] & 0xFFFF0000u));
+                w[e] = lo | (hi << 16);
+            }
+            uint4 o;
+            if (pair_order) {
+                o.x = prmt(w[0], w[2], 0x5410u);
+                o.y = prmt(w[0], w[2], 0x7632u);
+                o.z = prmt(w[1], w[3], 0x5410u);
+                o.w = prmt(w[1], w[3], 0x7632u);
+            } else {
+                o = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            *reinterpret_cast<uint4 *>(dst + static_cast<int64_t>(m) * ld_dst + k0) = o;
+        }
+    }
+}
+
 }  // namespace qmv
+
+cudaError_t launch_resid_norm(float *h, int64_t ld_h, const float *add, int64_t ld_add, const uint16_t *gamma,
+                              float eps, int M, int K, int bits, uint16_t *dst, int64_t ld_dst, cudaStream_t stream,
+                              bool pdl) {
+    const int per = (K + 2047) / 2048;  // 8 columns per thread per pass, 256 threads
+    const int po = bits == 4 ? 1 : 0;
+    cudaError_t e;
+    switch (per) {
+    case 1: e = launch_ex(qmv::resid_norm_kernel<1>, dim3(M), dim3(256), 0, stream, false, pdl, h, ld_h, add, ld_add,
+                          gamma, eps, K, po, dst, ld_dst); break;
+    case 2: e = launch_ex(qmv::resid_norm_kernel<2>, dim3(M), dim3(256), 0, stream, false, pdl, h, ld_h, add, ld_add,
+                          gamma, eps, K, po, dst, ld_dst); break;
+    case 3:
+    case 4: e = launch_ex(qmv::resid_norm_kernel<4>, dim3(M), dim3(256), 0, stream, false, pdl, h, ld_h, add, ld_add,
+                          gamma, eps, K, po, dst, ld_dst); break;
+    default: return cudaErrorInvalidValue;
+    }
+    count_launch();
+    return e;
+}
 
 bool qmv_supported(const QmmArgs &a, const char **why) {
     auto no = [&](const char *r) { if (why) *why = r; return false; };
     if (a.bits != 4 && a.bits != 8) return no("qmv: bits must be 4 or 8");
     if (a.group != 64) return no("qmv: group_size must be 64");
     if (!a.x_bf16 || !a.p_bf16) return no("qmv: activations and parameters must be bf16");
-    if (a.M > 16) return no("qmv: M > 16");
-    if (a.K % 512) return no("qmv: K must be a multiple of 512");
+    if (a.M > kMaxQmvRows) return no("qmv: M > 32");
+    if (a.K % (a.bits == 4 ? 256 : 128)) return no("qmv: K must be a multiple of the 128-byte packed stage");
     if (a.x.col_stride != 1 || a.w.col_stride != 1 || a.s.col_stride != 1 || a.b.col_stride != 1)
         return no("qmv: inputs need unit column stride");
     auto al = [](const void *p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
@@ -707,7 +855,7 @@ bool qmv_supported(const QmmArgs &a, const char **why) {
     if (!al(a.w.ptr, 16) || (a.w.row_stride * 4) % 16) return no("qmv: packed rows must be 16-byte aligned");
     if (!al(a.s.ptr, 16) || !al(a.b.ptr, 16) || (a.s.row_stride * 2) % 16 || (a.b.row_stride * 2) % 16)
         return no("qmv: parameter rows must be 16-byte aligned");
-    if ((a.N + qmv::ROWS - 1) / qmv::ROWS > kMaxTiles / 2) return no("qmv: N beyond the arrival-counter region");
+    if ((a.N + 159) / 160 > kMaxTiles / 2) return no("qmv: N beyond the arrival-counter region");
     if (a.N >= (int64_t(1) << 31) || a.K >= (int64_t(1) << 30)) return no("qmv: size beyond 32-bit indexing");
     return true;
 }
@@ -715,38 +863,72 @@ bool qmv_supported(const QmmArgs &a, const char **why) {
 namespace {
 
 constexpr int kSmemCap = 227 * 1024;
-constexpr int kOverhead = 1024 + qmv::MAX_STAGES * 4 * 16 * 4 + 3 * qmv::MAX_STAGES * 8 + 64;
+constexpr int kOverhead = 1024 + qmv::MAX_STAGES * 4 * qmv::MAX_XR * 4 + 3 * qmv::MAX_STAGES * 8 + 64;
 
-int stage_bytes(int bits) { return bits == 4 ? qmv::Shape<4>::BYTES : qmv::Shape<8>::BYTES; }
+int stage_bytes(int bits, int variant) {
+    switch (variant) {
+    case 0: return bits == 4 ? qmv::Shape<4, 1, 2, 12>::BYTES : qmv::Shape<8, 1, 2, 12>::BYTES;
+    case 1: return bits == 4 ? qmv::Shape<4, 1, 1, 12>::BYTES : qmv::Shape<8, 1, 1, 12>::BYTES;
+    case 2: return bits == 4 ? qmv::Shape<4, 2, 2, 10>::BYTES : qmv::Shape<8, 2, 2, 10>::BYTES;
+    case 3: return bits == 4 ? qmv::Shape<4, 2, 1, 10>::BYTES : qmv::Shape<8, 2, 1, 10>::BYTES;
+    default: return bits == 4 ? qmv::Shape<4, 4, 1, 10>::BYTES : qmv::Shape<8, 4, 1, 10>::BYTES;
+    }
+}
 
 }  // namespace
 
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
-    QmvPlan p{};
-    const int sb = stage_bytes(a.bits);
-    const int stages = std::min(qmv::MAX_STAGES, (kSmemCap - kOverhead) / sb);
-    if (stages < 2) return p;
-    const int64_t nblocks = (a.N + qmv::ROWS - 1) / qmv::ROWS;
+    // Candidates for this M; each is scored by its makespan in weight
+    // row-stages (items per CTA x block rows), with one-tile-per-warp variants
+    // charged 12% for their lower activation-fragment reuse (measured consumer
+    // rates 64% vs 72% of the HBM rate at M = 16).
+    int cand[2], nc = 0;
+    if (a.M > 16) {
+        cand[nc++] = 4;
+    } else if (a.M > 8) {
+        cand[nc++] = 2;
+        cand[nc++] = 3;
+    } else {
+        cand[nc++] = 0;
+        cand[nc++] = 1;
+    }
     const int kps = a.bits == 4 ? 256 : 128;
     const int64_t spb = a.K / kps;
-    const int64_t items = nblocks * spb;
-    // The fewest CTAs with the makespan of one per SM: fewer contributors per
-    // block, less partial traffic.
-    const int64_t per_sm = (items + num_sms - 1) / num_sms;
-    const int grid = static_cast<int>((items + per_sm - 1) / per_sm);
-    // Contributors per block: a block spans at most ceil(spb / floor(items/grid)) + 1 CTAs.
-    const int64_t per_cta = std::max<int64_t>(1, items / grid);
-    const int max_slots = static_cast<int>(std::min<int64_t>((spb + per_cta - 1) / per_cta + 1, grid));
-    const size_t need = kPartialOffset + static_cast<size_t>(nblocks) * max_slots * a.M * qmv::ROWS * 4 +
-                        qmv_prep_bytes(a);
-    if (need > workspace_bytes) return p;
-    p.splits = 1;
-    p.ks = static_cast<int>(a.K);
-    p.grid_n = grid;
-    p.stages = stages;
-    p.max_slots = max_slots;
-    p.smem_bytes = kOverhead + stages * sb;
-    return p;
+    QmvPlan best{};
+    double best_cost = 0.0;
+    for (int ci = 0; ci < nc; ++ci) {
+        const int v = cand[ci];
+        const int sb = stage_bytes(a.bits, v);
+        const int stages = std::min(qmv::MAX_STAGES, (kSmemCap - kOverhead) / sb);
+        if (stages < 2) continue;
+        const int rows = qmv::kVariantRows[v];
+        const int64_t nblocks = (a.N + rows - 1) / rows;
+        const int64_t items = nblocks * spb;
+        // The fewest CTAs with the makespan of one per SM: fewer contributors
+        // per block, less partial traffic.
+        const int64_t per_sm = (items + num_sms - 1) / num_sms;
+        const int grid = static_cast<int>((items + per_sm - 1) / per_sm);
+        // Contributors per block: a block spans at most ceil(spb / floor(items/grid)) + 1 CTAs.
+        const int64_t per_cta = std::max<int64_t>(1, items / grid);
+        const int max_slots = static_cast<int>(std::min<int64_t>((spb + per_cta - 1) / per_cta + 1, grid));
+        const size_t need = kPartialOffset + static_cast<size_t>(nblocks) * max_slots * a.M * rows * 4 +
+                            qmv_prep_bytes(a);
+        if (need > workspace_bytes) continue;
+        const double cost = double(per_sm) * rows * (qmv::kVariantNT[v] == 1 ? 1.12 : 1.0);
+        if (best.splits && cost >= best_cost) continue;
+        QmvPlan p{};
+        p.splits = 1;
+        p.ks = static_cast<int>(a.K);
+        p.grid_n = grid;
+        p.stages = stages;
+        p.max_slots = max_slots;
+        p.smem_bytes = kOverhead + stages * sb;
+        p.variant = v;
+        p.rows = rows;
+        best = p;
+        best_cost = cost;
+    }
+    return best;
 }
 
 size_t qmv_prep_bytes(const QmmArgs &a) {
@@ -756,47 +938,52 @@ size_t qmv_prep_bytes(const QmmArgs &a) {
 }
 
 size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p) {
-    const int64_t nblocks = (a.N + qmv::ROWS - 1) / qmv::ROWS;
-    return kPartialOffset + static_cast<size_t>(nblocks) * p.max_slots * a.M * qmv::ROWS * 4 + qmv_prep_bytes(a);
+    const int rows = p.rows;
+    const int64_t nblocks = (a.N + rows - 1) / rows;
+    return kPartialOffset + static_cast<size_t>(nblocks) * p.max_slots * a.M * rows * 4 + qmv_prep_bytes(a);
 }
 
-template <int BITS, int MT>
+namespace {
+std::atomic<uint64_t> g_arrival_wait_ns{kArrivalWaitNs};
+std::atomic<unsigned> g_extra_arrivals{0};
+}  // namespace
+
+void qmv_set_combine_wait(uint64_t limit_ns, unsigned extra_arrivals) {
+    g_arrival_wait_ns.store(limit_ns ? limit_ns : kArrivalWaitNs);
+    g_extra_arrivals.store(extra_arrivals);
+}
+
+template <int BITS, int MT, int NT, int CW>
 static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, const CUtensorMap &bm,
-                              const CUtensorMap &xm, const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream) {
-    auto kern = qmv::qmv_kernel<BITS, MT>;
+                              const CUtensorMap &xm, const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream,
+                              bool pdl) {
+    auto kern = qmv::qmv_kernel<BITS, MT, NT, CW>;
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(kern), plan.smem_bytes);
     if (e != cudaSuccess) return e;
-    // Cooperative: every CTA is resident, so the combine phase may wait for
-    // the other contributors of a block.
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(plan.grid_n);
-    cfg.blockDim = dim3(qmv::THREADS);
-    cfg.dynamicSmemBytes = plan.smem_bytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, wm, sm, bm, xm, p);
+    // Every CTA must be resident for the combine phase: a cooperative launch
+    // guarantees it.  With programmatic dependent launch the grid (at most one
+    // CTA per SM) becomes resident as the preceding kernel's CTAs leave; the
+    // next kernel launches only after every CTA of this grid has started.
+    e = launch_ex(kern, dim3(plan.grid_n), dim3(qmv::Shape<BITS, MT, NT, CW>::THREADS), plan.smem_bytes, stream, !pdl,
+                  pdl, wm, sm, bm, xm, p);
     count_launch();
     return e;
 }
 
 cudaError_t launch_qmv_prep(const void *src, int64_t ld_src, int mode, const float *ss, int ss_tiles,
                             const uint16_t *gamma, float eps, int M, int K, int bits, uint16_t *dst, int64_t ld_dst,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, bool pdl) {
     const int64_t words = static_cast<int64_t>(M) * (K / 8);
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<int64_t>((words + threads - 1) / threads, 1184));
-    qmv::prep_kernel<<<blocks, threads, 0, stream>>>(src, ld_src, mode, ss, ss_tiles, gamma, eps, M, K, bits == 4 ? 1 : 0,
-                                                     dst, ld_dst);
+    cudaError_t e = launch_ex(qmv::prep_kernel, dim3(blocks), dim3(threads), 0, stream, false, pdl, src, ld_src, mode,
+                              ss, ss_tiles, gamma, eps, M, K, bits == 4 ? 1 : 0, dst, ld_dst);
     count_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, cudaStream_t stream,
-                       const QmvFusion *fusion) {
+                       const QmvFusion *fusion, bool pdl) {
     if (plan.splits < 1) return cudaErrorInvalidValue;
     qmv::Params p{};
     p.y = a.y;
@@ -804,12 +991,15 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     p.M = static_cast<int>(a.M);
     p.N = static_cast<int>(a.N);
     p.K = static_cast<int>(a.K);
-    p.nblocks = static_cast<int>((a.N + qmv::ROWS - 1) / qmv::ROWS);
+    const int rows = plan.rows;
+    p.nblocks = static_cast<int>((a.N + rows - 1) / rows);
     p.spb = static_cast<int>(a.K / (a.bits == 4 ? 256 : 128));
     p.items = static_cast<int64_t>(p.nblocks) * p.spb;
     p.stages = plan.stages;
     p.max_slots = plan.max_slots;
     p.y_bf16 = a.y_bf16;
+    p.arrival_wait_ns = g_arrival_wait_ns.load();
+    p.extra_arrivals = g_extra_arrivals.load();
     if (fusion) p.f = *fusion;
     char *ws = static_cast<char *>(workspace);
     p.status = reinterpret_cast<unsigned *>(ws);
@@ -823,27 +1013,37 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     if (a.bits == 4 && !in_order) {
         uint16_t *dst = reinterpret_cast<uint16_t *>(ws + qmv_workspace_bytes(a, plan) - qmv_prep_bytes(a));
         cudaError_t e = launch_qmv_prep(a.x.ptr, a.x.row_stride, 0, nullptr, 0, nullptr, 0.f, p.M, p.K, 4, dst, p.K,
-                                        stream);
+                                        stream, pdl);
         if (e != cudaSuccess) return e;
         xq = dst;
         ldxq = p.K;
     }
     const CUtensorMap *wm, *sm, *bm, *xm;
     const uint64_t words = static_cast<uint64_t>(a.K) * a.bits / 32;
+    const uint32_t xr = a.M > 16 ? 32 : 16;
+    const uint32_t box_rows = plan.variant >= 2 ? 160 : 192;  // 16 rows per consumer warp
     if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32,
-                                    qmv::BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+                                    box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
         !(sm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2, 8,
-                                    qmv::BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+                                    box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
         !(bm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2, 8,
-                                    qmv::BOX_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-        !(xm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xq, a.K, a.M, ldxq * 2, 64, 16,
+                                    box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+        !(xm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xq, a.K, a.M, ldxq * 2, 64, xr,
                                     CU_TENSOR_MAP_SWIZZLE_128B)))
         return cudaErrorInvalidValue;
-    if (a.M > 8)
-        return a.bits == 4 ? launch_cfg<4, 2>(*wm, *sm, *bm, *xm, p, plan, stream)
-                           : launch_cfg<8, 2>(*wm, *sm, *bm, *xm, p, plan, stream);
-    return a.bits == 4 ? launch_cfg<4, 1>(*wm, *sm, *bm, *xm, p, plan, stream)
-                       : launch_cfg<8, 1>(*wm, *sm, *bm, *xm, p, plan, stream);
+    const bool b4 = a.bits == 4;
+    switch (plan.variant) {
+    case 0: return b4 ? launch_cfg<4, 1, 2, 12>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                      : launch_cfg<8, 1, 2, 12>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
+    case 1: return b4 ? launch_cfg<4, 1, 1, 12>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                      : launch_cfg<8, 1, 1, 12>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
+    case 2: return b4 ? launch_cfg<4, 2, 2, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                      : launch_cfg<8, 2, 2, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
+    case 3: return b4 ? launch_cfg<4, 2, 1, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                      : launch_cfg<8, 2, 1, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
+    default: return b4 ? launch_cfg<4, 4, 1, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                       : launch_cfg<8, 4, 1, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
+    }
 }
 
 }  // namespace afb

@@ -11,9 +11,16 @@
 
 namespace afb {
 
-// Error word written by device code when a bounded wait gives up; the host
-// reads it through affon_b200_ctx_synchronize().
-enum DeviceStatus : unsigned { DEV_OK = 0, DEV_TIMEOUT = 4 };
+// Error word written by device code; the host reads it through
+// affon_b200_ctx_synchronize().  DEV_TIMEOUT: a bounded wait gave up;
+// DEV_BOUNDS: a kernel read an index from device memory (a position, a token)
+// that lies outside its buffer and skipped the access.
+enum DeviceStatus : unsigned { DEV_OK = 0, DEV_TIMEOUT = 4, DEV_BOUNDS = 5 };
+
+// Limits of the bounded waits: a pipeline-stage wait (mbarrier) and a wait on
+// another CTA's or another GPU's arrival count.
+constexpr uint64_t kStageWaitNs = 4000000000ull;
+constexpr uint64_t kArrivalWaitNs = 4000000000ull;
 
 AFB_DEVICE uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -52,7 +59,7 @@ AFB_DEVICE bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // device status word, and returns false.  Every other waiter sees *abort and
 // leaves too, so no thread spins forever.
 AFB_DEVICE bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *status,
-                          uint64_t limit_ns = 4000000000ull) {
+                          uint64_t limit_ns = kStageWaitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t start = globaltimer();
     for (uint32_t i = 1;; ++i) {
@@ -90,6 +97,15 @@ AFB_DEVICE void tma_load_2d(void *smem_dst, const CUtensorMap *map, uint64_t *ba
 AFB_DEVICE void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+
+// Programmatic dependent launch (the kernel was launched with the
+// programmatic-stream-serialization attribute): pdl_wait() blocks until the
+// preceding kernel in the stream has completed and its memory is visible;
+// pdl_launch_dependents() lets the next kernel start launching once every CTA
+// of this grid has issued it (or exited).  Both are no-ops without the
+// attribute.
+AFB_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+AFB_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Named barrier among `threads` threads (id 1..15; id 0 is __syncthreads).
 AFB_DEVICE void named_bar_sync(int id, int threads) {
@@ -173,4 +189,31 @@ const CUtensorMap *cached_tensor_map_2d(CUtensorMapDataType dtype, const void *b
                                         CUtensorMapSwizzle swizzle);
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device, size).
 cudaError_t ensure_smem_attr(const void *kernel, int bytes);
+
+// cudaLaunchKernelEx with the optional cooperative (every CTA resident at
+// once) and programmatic-dependent-launch attributes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool coop,
+                      bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    if (coop) {
+        attr[n].id = cudaLaunchAttributeCooperative;
+        attr[n].val.cooperative = 1;
+        ++n;
+    }
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 }  // namespace afb

@@ -266,6 +266,117 @@ def _graph_time_ms(fn, reps, dev):
     return e0.elapsed_time(e1) / reps
 
 
+def ncu_traffic(key):
+    """Per-launch DRAM bytes (read + write) of a kernel from the committed ncu
+    summary, or None."""
+    tf = ROOT / "profiles" / "ncu_traffic.json"
+    if not tf.exists():
+        return None
+    ent = json.loads(tf.read_text()).get(key)
+    return ent.get("bytes_per_launch") if isinstance(ent, dict) else ent
+
+
+def kernel_keys(dev, pk):
+    """Stand-alone kernel figures measured in the same run: the LM-head qmv
+    (M=1 and M=16, 4-bit, N=128256, K=4096) in GB/s against HBM, and the
+    tcgen05 prefill qmm (4-bit, N=14336, K=4096, M=2048 and 8192, bf16
+    result) in TFLOP/s against the dense bf16 peak."""
+    import ctypes
+    import torch
+    from affon_b200 import _lib
+    from affon_b200.core import check
+    L = _lib.lib()
+    ctx = ctypes.c_void_p()
+    check(L.affon_b200_ctx_create(dev.index, None, ctypes.byref(ctx)))
+    out = {}
+    try:
+        N, K, bits, group = 128256, 4096, 4, 64
+        x, sets = make_qmv_operands(dev, 16, N, K, bits, group, copies=2, seed=3)
+        for M in (1, 16):
+            y = torch.empty((M, N), dtype=torch.float32, device=dev)
+            d = _qmm_desc(M, N, K, bits, group, "f32")
+            idx = [0]
+
+            def launch(s, M=M, d=d, y=y):
+                w, sc, b = sets[idx[0] % len(sets)]
+                idx[0] += 1
+                check(L.affon_b200_ctx_set_stream(ctx, s.cuda_stream))
+                check(L.affon_b200_qmm(ctx, ctypes.byref(d), x.data_ptr(), w.data_ptr(), sc.data_ptr(),
+                                       b.data_ptr(), y.data_ptr()))
+            ms = _graph_time_ms(launch, 20, dev)
+            nbytes = qmv_bytes(M, N, K, bits, group, 4)
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            out[f"qmv_lm_head_m{M}_b4"] = {"GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 4),
+                                           "us_per_launch": round(ms * 1e3, 2), "bytes_per_launch": nbytes,
+                                           "shape": f"M={M} N={N} K={K} 4-bit g64, f32 result, 2 weight copies rotated"}
+        del sets, x
+        N, K = 14336, 4096
+        _, sets = make_qmv_operands(dev, 1, N, K, bits, group, copies=1, seed=4)
+        w, sc, b = sets[0]
+        for M in (2048, 8192):
+            xm = torch.randn((M, K), device=dev).to(torch.bfloat16)
+            y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            d = _qmm_desc(M, N, K, bits, group, "bf16")
+            sel = _lib.Selection()
+            check(L.affon_b200_ctx_set_stream(ctx, torch.cuda.current_stream(dev).cuda_stream))
+            check(L.affon_b200_qmm_explain(ctx, ctypes.byref(d), xm.data_ptr(), w.data_ptr(), sc.data_ptr(),
+                                           b.data_ptr(), y.data_ptr(), ctypes.byref(sel)))
+
+            def launch(s, d=d, xm=xm, y=y):
+                check(L.affon_b200_ctx_set_stream(ctx, s.cuda_stream))
+                check(L.affon_b200_qmm(ctx, ctypes.byref(d), xm.data_ptr(), w.data_ptr(), sc.data_ptr(),
+                                       b.data_ptr(), y.data_ptr()))
+            ms = _graph_time_ms(launch, 5, dev)
+            tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            out[f"qmm_tc_m{M}_n{N}_k{K}_b4"] = {
+                "TFLOP/s": round(tf, 1), "frac_of_measured_bf16": round(tf / pk["bf16_tflops"], 4),
+                "ms_per_launch": round(ms, 4), "implementation": sel.implementation_id.decode(),
+                "shape": f"M={M} N={N} K={K} 4-bit g64, bf16 result"}
+            del xm, y
+    finally:
+        L.affon_b200_ctx_destroy(ctx)
+    return out
+
+
+def _qmm_desc(M, N, K, bits, group, yd):
+    import ctypes
+    from affon_b200 import _lib
+    per = 32 // bits
+    d = _lib.QmmDesc()
+    d.struct_size = ctypes.sizeof(_lib.QmmDesc)
+    d.bits, d.group_size = bits, group
+    d.x_dtype = d.param_dtype = _lib.BF16
+    d.y_dtype = _lib.F32 if yd == "f32" else _lib.BF16
+    d.x = _lib.View(M, K, K, 1, 0)
+    d.w = _lib.View(N, K // per, K // per, 1, 0)
+    d.s = d.b = _lib.View(N, K // group, K // group, 1, 0)
+    d.y = _lib.View(M, N, N, 1, 0)
+    return d
+
+
+# Algorithmic HBM bytes per decode step by kernel role (the roofline unit):
+# each projection streams its packed codes plus bf16 scales and biases once;
+# attention reads the K and V rows of every cached position.
+def role_bytes(dec, pos):
+    from affon_b200.decoder import weight_bytes
+    c, B = dec.cfg, dec.B
+    lin = lambda l: l.N * l.K * l.bits // 8 + l.N * (l.K // l.group) * 4
+    per = {k: sum(lin(lay[k]) for lay in dec.layers) for k in ("qkv", "o", "gate_up", "down")}
+    per["lm_head"] = lin(dec.lm_head)
+    per["attn"] = 2 * B * dec.kv_heads_local * (pos + 1) * c.head_dim * 2 * c.layers
+    return per
+
+
+def group_id(rank, world):
+    """rank 0 makes the tensor-parallel group id; every rank receives it over
+    the benchmark's own process group."""
+    import torch.distributed as dist
+    from affon_b200 import tp as tpmod
+    obj = [tpmod.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
 def run_decode(args, rank, world, dev):
     import ctypes
     import torch
@@ -277,20 +388,21 @@ def run_decode(args, rank, world, dev):
     cfg = LLAMA3_8B
     B, ctxlen = 16, 1024
     cap = ctxlen + args.warmup + 2 * args.steps + 8
-    dec = QuantizedDecoder(cfg, B, cap, dev, seed=0, max_steps=args.warmup + 2 * args.steps + 8)
+    tp = (rank, world, group_id(rank, world), 120.0) if world > 1 else None
+    dec = QuantizedDecoder(cfg, B, cap, dev, seed=0, max_steps=args.warmup + 2 * args.steps + 8, tp=tp)
     gen = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (ctxlen, B), generator=gen)
     dec.capture()
     t0 = time.time()
     dec.prefill(prompt)                     # positions 0..1023 through the same graph
-    torch.cuda.synchronize(dev)
+    dec.synchronize(120.0)
     prefill_s = time.time() - t0
     dec.reset(ctxlen)
     L = _lib.lib()
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         dec.replay()
-    torch.cuda.synchronize(dev)
+    dec.synchronize(120.0)
     if world > 1:
         dist.barrier()
     pos0 = int(dec.pos.item())
@@ -298,10 +410,12 @@ def run_decode(args, rank, world, dev):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clocks:
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("bench_timed")
         ev0.record(stream)
         for _ in range(args.steps):
             dec.replay()
         ev1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(dev)
     ms = ev0.elapsed_time(ev1) / args.steps
     # graph replays do not pass through the C ABI, so count the launches of one
@@ -313,11 +427,11 @@ def run_decode(args, rank, world, dev):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
-    tok_s = B * world / (ms_max * 1e-3)
+    tok_s = B / (ms_max * 1e-3)            # tensor parallel: all ranks serve the same batch
     # bytes per step at the mean position of the timed steps
     mid = pos0 + args.steps // 2
-    step_bytes = dec.step_bytes(mid)
-    wbytes = weight_bytes(cfg)
+    step_bytes = dec.step_bytes(mid)       # this rank's shard of the weights + its KV heads
+    wbytes = weight_bytes(cfg) // world
 
     # e2e: each step copies its input tokens from pinned host memory and reads
     # the sampled tokens back, inside the timed region.
@@ -341,37 +455,57 @@ def run_decode(args, rank, world, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    # dominant kernel, timed live: the gate/up qmv (largest share of the weight
-    # bytes) with its silu*mul epilogue, reading the normalized activations
-    lay = dec.layers[0]
-    gu = lay["gate_up"]
-    desc = gu.desc(B)
-    fus = None
-    for call in dec.calls:
-        if call[0] == "qmv" and call[3] is gu:
-            fus = call[5]
-    # rotate over all 32 layers' gate/up weights so launches stream from HBM
-    gus = [l["gate_up"] for l in dec.layers]
-    idx = [0]
-    def gu_launch_rot(s):
-        lin = gus[idx[0] % len(gus)]
-        idx[0] += 1
-        check(L.affon_b200_ctx_set_stream(dec.ctx, s.cuda_stream))
-        check(L.affon_b200_qmv_fused(dec.ctx, ctypes.byref(desc), dec.xq.data_ptr(), lin.w.data_ptr(),
-                                     lin.s.data_ptr(), lin.b.data_ptr(), None, ctypes.byref(fus)))
-    gu_ms = _graph_time_ms(gu_launch_rot, 64, dev)
+    # The same timed replays with programmatic dependent launch off (graph
+    # recaptured), to show what the overlap between kernels buys.
+    check(L.affon_b200_ctx_set_overlap(dec.ctx, 0))
+    dec.capture()
+    dec.reset(pos0)
+    for _ in range(2):
+        dec.replay()
+    dec.reset(pos0)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(args.steps):
+        dec.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    off_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([off_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        off_ms = float(t.item())
+    check(L.affon_b200_ctx_set_overlap(dec.ctx, 1))
+    dec.capture()
+    dec.reset(pos0 + args.steps)
+
+    # Per-kernel breakdown of one step: every role's launch timed alone in a
+    # CUDA graph of back-to-back launches rotating over the 32 layers' weights
+    # (or KV caches), times its launches per step.  The dominant kernel is the
+    # one with the largest share; its graph-timed launch is the roofline line.
+    breakdown = dec.step_breakdown()
+    per_step = {"qkv": cfg.layers, "o": cfg.layers, "gate_up": cfg.layers, "down": cfg.layers,
+                "attn": cfg.layers, "lm_head": 1}
+    bytes_role = role_bytes(dec, mid)
+    total_bd = sum(v[0] for v in breakdown.values())
+    dominant = max((r for r in per_step), key=lambda r: breakdown.get(r, (0.0, 0))[0])
+    dom_ms = breakdown[dominant][0] / breakdown[dominant][1]
+    dom_bytes = bytes_role[dominant] // per_step[dominant]
+    dom_name = role_kernel_name(dec, dominant)
     dec.set_stream(torch.cuda.current_stream(dev))
-    gu_bytes = gu.N * gu.K * gu.bits // 8 + gu.N * (gu.K // 64) * 4 + B * gu.K * 2 + B * (gu.N // 2) * 2
     dec.close()
+    del dec
+    torch.cuda.empty_cache()
+    config5 = run_config5(args, rank, world, dev) if not args.no_config5 else None
 
     pk, pk_kind = peaks()
     roof_tok_s = B / (step_bytes / (pk["hbm_gbs"] * 1e9))
     roof_w_tok_s = B / (wbytes / (pk["hbm_gbs"] * 1e9))
-    gu_achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "ncu_traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get("qmv_gate_up_m16_b4_n28672_k4096")
+    dom_achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    bd = {r: {"ms_per_step": round(t, 4), "launches": n, "us_per_launch": round(t / n * 1e3, 2),
+              "share": round(t / total_bd, 4),
+              "GB/s": round(bytes_role[r] / (t * 1e-3) / 1e9, 1) if r in bytes_role and t > 0 else None}
+          for r, (t, n) in sorted(breakdown.items(), key=lambda kv: -kv[1][0])}
+    kernels = kernel_keys(dev, pk) if not args.no_kernel_keys and world == 1 else {}
     return {
         "metric": "4-bit decode tok/s (Llama-3-8B shape, batch 16, 1024 context)", "value": round(tok_s, 1),
         "unit": "tok/s", "ms_per_step": round(ms_max, 4), "higher_is_better": True,
@@ -379,24 +513,103 @@ def run_decode(args, rank, world, dev):
         "config": {"workload": "decode_llama3_8b_b16_ctx1024", "model": "llama3-8b-shape (random init, 4-bit g64)",
                    "global_batch": B, "seq_len": ctxlen, "layers": cfg.layers, "d_model": cfg.d_model,
                    "ffn": cfg.ffn, "vocab": cfg.vocab, "kv_cache": "prefilled by 1024 teacher-forced decode steps",
-                   "prefill_seconds": round(prefill_s, 2), "l2": "weights 4.2 GB >> L2",
+                   "prefill_seconds": round(prefill_s, 2), "l2": "weights 4.2 GB >> L2 (no L2 flush needed)",
                    "step_hbm_bytes": step_bytes, "weight_bytes": wbytes,
                    "roofline_tok_s_weights_plus_kv": round(roof_tok_s, 1),
-                   "frac_of_weights_plus_kv_roofline": round(tok_s / world / roof_tok_s, 4),
+                   "frac_of_weights_plus_kv_roofline": round(tok_s / roof_tok_s, 4),
                    "roofline_tok_s_weights_only": round(roof_w_tok_s, 1),
-                   "frac_of_weights_only_roofline": round(tok_s / world / roof_w_tok_s, 4),
-                   "step_achieved_gbs": round(step_bytes / (ms_max * 1e-3) / 1e9, 1)},
-        "e2e": {"value": round(B * world / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 4,
+                   "frac_of_weights_only_roofline": round(tok_s / roof_w_tok_s, 4),
+                   "step_achieved_gbs": round(step_bytes / (ms_max * 1e-3) / 1e9, 1),
+                   "overlap": "programmatic dependent launch between the step's kernels",
+                   "ms_per_step_overlap_off": round(off_ms, 4)},
+        "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 4,
                 "d2h_bytes_per_step": B * 4, "ms_per_step": round(e2e_ms, 4),
                 "path": "decoder graph replay with pinned token H2D/D2H and host read each step"},
-        "roofline": {"bound": "hbm", "kernel": "qmv gate/up (silu*mul epilogue), M=16 N=28672 K=4096",
-                     "achieved": round(gu_achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(gu_achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+        "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(dom_achieved, 1),
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(dom_achieved / pk["hbm_gbs"], 4),
+                     "traffic": ncu_traffic(ROLE_TRAFFIC_KEY[dominant]),
                      "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json)" if pk_kind == "measured" else
-                     "fallback 6.65 TB/s", "algorithmic_bytes_per_launch": gu_bytes,
-                     "launch_us": round(gu_ms * 1e3, 2)},
+                     "fallback 6.65 TB/s", "algorithmic_bytes_per_launch": dom_bytes,
+                     "launch_us": round(dom_ms * 1e3, 2)},
+        "breakdown": {"per_role": bd, "sum_of_kernels_ms": round(total_bd, 4), "graph_step_ms": round(ms_max, 4),
+                      "how": "each role's launches timed alone: a CUDA graph of back-to-back launches rotating "
+                             "over the layers' weights or KV caches, overlap off; x launches per step"},
+        "kernels": kernels,
+        "config5_70b": config5,
         "gpu_launches": int(launches), "clocks": clocks.summary(), "_rank0_ms": ms,
     }
+
+
+def role_kernel_name(dec, role):
+    c = dec.cfg
+    if role == "attn":
+        return (f"decode attention (RoPE + KV append), batch {dec.B}, {dec.kv_heads_local} KV heads x "
+                f"{c.q_heads // c.kv_heads} query heads, ctx ~{int(dec.pos.item())}")
+    lin = dec.lm_head if role == "lm_head" else dec.layers[0][role]
+    epi = {"gate_up": " (silu*mul epilogue)", "o": " (residual epilogue)", "down": " (residual epilogue)",
+           "lm_head": " (argmax epilogue)"}.get(role, "")
+    if dec.world > 1 and role in ("o", "down"):
+        epi = " (row-parallel partial, f32)"
+    return f"qmv {role}{epi}, M={dec.B} N={lin.N} K={lin.K} {lin.bits}-bit"
+
+
+ROLE_TRAFFIC_KEY = {
+    "gate_up": "qmv_gate_up_m16_b4_n28672_k4096", "down": "qmv_down_m16_b4_n4096_k14336",
+    "qkv": "qmv_qkv_m16_b4_n6144_k4096", "o": "qmv_o_m16_b4_n4096_k4096", "lm_head": "qmv_lm_head_m16_b4",
+    "attn": "decode_attention_b16_kvh8_g4_ctx1024",
+}
+
+
+def run_config5(args, rank, world, dev):
+    """the Llama-3-70B shape (80 layers, d 8192, 64/8
+    heads, FFN 28672, vocab 128256), 4-bit, batch 32 at a 2048-token context,
+    tensor-parallel over the job's GPUs.  The KV cache is filled with random
+    values instead of running 2048 teacher-forced steps (the step's cost does
+    not depend on the cached values).  Device-timed decode tok/s, max over
+    ranks."""
+    import torch
+    import torch.distributed as dist
+    from affon_b200.decoder import LLAMA3_70B, QuantizedDecoder, weight_bytes
+    cfg, B, ctxlen = LLAMA3_70B, 32, 2048
+    try:
+        tp = (rank, world, group_id(rank, world), 120.0) if world > 1 else None
+        dec = QuantizedDecoder(cfg, B, ctxlen + args.warmup + args.steps + 4, dev, seed=5, max_steps=8, tp=tp)
+    except Exception as e:  # e.g. not enough memory: report, keep the main line
+        return {"error": f"{type(e).__name__}: {e}"[:300]}
+    try:
+        dec.fill_kv_random(ctxlen)
+        dec.capture()
+        for _ in range(args.warmup):
+            dec.replay()
+        dec.synchronize(120.0)
+        if world > 1:
+            dist.barrier()
+        stream = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            dec.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        pk, _ = peaks()
+        step_bytes = dec.step_bytes(ctxlen + args.warmup + args.steps // 2)
+        roof = B / (step_bytes / (pk["hbm_gbs"] * 1e9))
+        return {"metric": "4-bit decode tok/s (Llama-3-70B shape, batch 32, 2048 context)",
+                "value": round(B / (ms * 1e-3), 1), "unit": "tok/s", "ms_per_step": round(ms, 4),
+                "parallelism": f"tp{world}" if world > 1 else "single",
+                "step_hbm_bytes_per_gpu": step_bytes, "weight_bytes_per_gpu": weight_bytes(cfg) // world,
+                "roofline_tok_s_weights_plus_kv": round(roof, 1), "frac_of_weights_plus_kv_roofline":
+                round(B / (ms * 1e-3) / roof, 4), "kv_cache": "2048 positions of random bf16 values",
+                "launches_per_step": dec.launches_per_step()}
+    finally:
+        dec.close()
+        del dec
+        torch.cuda.empty_cache()
 
 
 def cpu_baseline_decode(args, threads, seconds_target=15.0):
@@ -421,7 +634,7 @@ def cpu_baseline_decode(args, threads, seconds_target=15.0):
             break
     t = statistics.median(times)
     step_s = t * linear_param_count(LLAMA3_8B) / (rows * K)
-    return {"value": round(M / step_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+    return {"value": round(M / step_s, 4), "unit": "tok/s", "cores": threads, "kind": "port", "cpu_model": cpu_model(),
             "sample": f"M=16 x {rows} weight rows x K=4096 (4-bit) per run, median of {len(times)} runs "
                       f"({t * 1e3:.1f} ms), scaled by the 7.5e9 linear weights of a step; attention and norms "
                       f"not counted"}
@@ -446,9 +659,19 @@ def cpu_baseline_qmv(args, threads, seconds_target=15.0):
             break
     t = statistics.median(times)
     nbytes = qmv_bytes(M, rows, K, bits, group, 4)
-    return {"value": round(nbytes / t / 1e9, 4), "unit": "GB/s", "cores": threads,
+    return {"value": round(nbytes / t / 1e9, 4), "unit": "GB/s", "cores": threads, "cpu_model": cpu_model(),
             "kind": "port", "sample": f"M={M}, {rows} of {cfg['N']} weight rows, K={K}, {bits}-bit; "
                                       f"median of {len(times)} runs, {t * 1e3:.1f} ms each"}
+
+
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 def host_threads():
@@ -464,8 +687,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="affon_b200", choices=["affon_b200", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "qmv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "qmv", "kernel", "sweep"])
+    ap.add_argument("--kernel", default="gate_up", choices=sorted(KERNEL_CASES) + ["attn", "qmm"],
+                    help="--workload kernel: which kernel to run alone")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernel-keys", action="store_true", help="skip the stand-alone qmv/qmm kernel figures")
+    ap.add_argument("--no-config5", action="store_true", help="skip the 70B (BASELINE config 5) extra key")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -487,7 +714,8 @@ def main():
             vals.append(base["value"])
         value = statistics.median(vals)
         line = {"metric": metric, "value": value, "unit": unit, "impl": "reference", "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                "scaling": "strong" if args.workload == "decode" else "weak",
                 "vs_baseline": None, "dtype": "f32 (bf16 widened)", "data": "synthetic",
                 "config": {"workload": workload}, "cpu_baseline": {**base, "value": value},
                 "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -504,12 +732,16 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.workload == "kernel":
+        return run_kernel(args, dev)
+    if args.workload == "sweep":
+        return run_sweep(args, dev)
     res = run_decode(args, rank, world, dev) if args.workload == "decode" else run_qmv(args, rank, world, dev)
     if rank == 0:
-        res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "scaling": "weak",
-                    "vs_baseline": None, "data": "synthetic (seeded random weights and tokens, BASELINE "
+        res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "scaling": "strong" if args.workload == "decode" else "weak", "vs_baseline": None, "data": "synthetic (seeded random weights and tokens, BASELINE "
                                                   "distributions)"})
-        res["config"]["parallelism"] = f"replicas{world}" if world > 1 else "single"
+        res["config"]["parallelism"] = f"tp{world}" if world > 1 else "single"
         if not args.no_cpu_baseline:
             res["cpu_baseline"] = (cpu_baseline_decode if args.workload == "decode" else cpu_baseline_qmv)(args, 1)
         res.pop("_rank0_ms", None)

@@ -47,7 +47,8 @@ typedef enum affon_b200_status {
 typedef enum affon_b200_dtype {
     AFFON_B200_F32 = 0,
     AFFON_B200_BF16 = 1,
-    AFFON_B200_U32 = 2
+    AFFON_B200_U32 = 2,
+    AFFON_B200_U64 = 3  /* tensor-parallel max-reduction of packed argmax keys */
 } affon_b200_dtype;
 
 /* CompileOptions.numericalPolicy (docs/core/optimization-and-profiling.md:124-130). */
@@ -120,13 +121,29 @@ int affon_b200_ctx_create(int device_ordinal, void *cuda_stream, affon_b200_ctx 
 int affon_b200_ctx_destroy(affon_b200_ctx *ctx);
 int affon_b200_ctx_set_stream(affon_b200_ctx *ctx, void *cuda_stream);
 int affon_b200_ctx_device(const affon_b200_ctx *ctx);
+/* Overlap mode (default off): launch the decode kernels (qmv, its prologue,
+ * decode attention, embed, finalize) with programmatic dependent launch, so
+ * each may start while the kernel before it in the stream finishes and
+ * prefetch its weights, scales and biases -- never its activations -- before
+ * waiting for that kernel.  Enable it only when no kernel launched directly
+ * before one of these writes its weights, scales or biases. */
+int affon_b200_ctx_set_overlap(affon_b200_ctx *ctx, int enable);
+
+/* Test hook of the decode qmv's split-K combine, process-wide: the limit of
+ * its bounded wait for the other contributors of a block (0 = the default
+ * 4 s) and arrivals it waits for beyond the real contributors (0 in normal
+ * use; 1 makes every shared block's wait run out, so a test can check that
+ * the timeout is reported and the next launch is correct). */
+int affon_b200_debug_set_combine_wait(uint64_t limit_ns, uint32_t extra_arrivals);
+
 /* Grow the workspace to at least `bytes` (allocates; never called implicitly
  * by a launch, so launches can be captured in CUDA graphs). */
 int affon_b200_ctx_reserve_workspace(affon_b200_ctx *ctx, size_t bytes);
 
-/* Wait for the context's stream and report device-side failures: returns
- * AFFON_B200_TIMEOUT (and clears the flag) when a kernel's bounded wait gave
- * up since the last check. */
+/* Wait for the context's stream and report device-side failures since the
+ * last check (and clear them): AFFON_B200_TIMEOUT when a kernel's bounded wait
+ * gave up, AFFON_B200_INVALID_ARG when a kernel found a device-resident
+ * position or token out of range. */
 int affon_b200_ctx_synchronize(affon_b200_ctx *ctx);
 
 /* Validation alone (program.ts:481-495 plus the descriptor's own checks). */
@@ -167,20 +184,27 @@ int affon_b200_compute_core_run_quantized_matmul_f32(
 /* Decode qmv without any device allocation.  (No counterpart in the
  * reference: an addition for callers that cannot let a library allocate
  * device memory -- runtimes that own all GPU memory in a pre-reserved arena,
- * plugin hosts whose allocator is the only one allowed to call the driver, or
- * code running while a stream is being captured.)  Same contract and results
- * as affon_b200_qmm for the decode qmv (M <= 16, 4/8-bit, group 64, bf16
- * activations and parameters); other descriptors return
- * AFFON_B200_UNSUPPORTED.  No context is needed: the launch goes to
- * `cuda_stream` on the current device, and the kernel's scratch lives in a
- * static 8 MiB device array that every GPU loading this library holds until
- * exit; shapes whose partial sums exceed it (large M*N) are rejected with
- * AFFON_B200_UNSUPPORTED and a message.  The first call on a device looks up
- * that array's device address, so make it before any stream capture.  All
- * calls share the one array: calls that overlap on the GPU (other streams,
- * other threads) race and must be serialised by the caller. */
+ * or plugin hosts whose allocator is the only one allowed to call the
+ * driver.)  Same contract and results as affon_b200_qmm for the decode qmv
+ * (M <= 32, 4/8-bit, group 64, bf16 activations and parameters); other
+ * descriptors return AFFON_B200_UNSUPPORTED.  No context is needed: the launch
+ * goes to `cuda_stream` on the current device, and the kernel's scratch lives
+ * in a static 8 MiB device array that every GPU loading this library holds
+ * until exit; shapes whose partial sums exceed it (large M*N) are rejected
+ * with AFFON_B200_UNSUPPORTED and a message.  The first call on a device looks
+ * up that array's device address, so make it before any stream capture.  All
+ * calls share the one array and each clears what must start at zero: calls
+ * that overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller. */
 int affon_b200_qmv_noalloc(const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w, const void *s,
                            const void *b, void *y, void *cuda_stream);
+
+/* Status of the last affon_b200_qmv_noalloc launch on the current device:
+ * synchronises `cuda_stream`, reads the static array's status word into
+ * *status_out (0 = fine) and returns AFFON_B200_TIMEOUT when a bounded wait of
+ * that launch gave up (its output is then invalid).  Read it before the next
+ * call, which clears the word.  Allocates nothing. */
+int affon_b200_qmv_noalloc_status(void *cuda_stream, uint32_t *status_out);
 
 /* ---------------------------------------------------------------------------
  * Decoder building blocks.  No counterpart in the reference, which has no
@@ -194,8 +218,8 @@ int affon_b200_qmv_noalloc(const affon_b200_qmm_desc *desc, const void *x, const
  * [x0 x4 x1 x5 x2 x6 x3 x7] (8-bit codes: natural order).  mode 0: src is
  * bf16 [rows][ld_src]; mode 1: src is an f32 residual stream h and the output
  * is bf16(h[m][k] * rsqrt(sum_k h[m][k]^2 / cols + eps) * gamma[k]), the sum
- * taken from ss ([ss_tiles][16] f32 partial sums, summed in a fixed order).
- * rows <= 16; dst is bf16 [rows][ld_dst]. */
+ * taken from ss ([ss_tiles][32] f32 partial sums, summed in a fixed order).
+ * rows <= 32; dst is bf16 [rows][ld_dst]. */
 int affon_b200_qmv_prep(affon_b200_ctx *ctx, int mode, const void *src, int64_t ld_src, const float *ss,
                         int ss_tiles, const void *gamma, float eps, int rows, int cols, int bits, void *dst,
                         int64_t ld_dst);
@@ -203,8 +227,8 @@ int affon_b200_qmv_prep(affon_b200_ctx *ctx, int mode, const void *src, int64_t 
 /* Fusions of the decode qmv.  x_mode 0: x is natural-order bf16 (the call
  * converts it); x_mode 1: x is already in the qmv's order (affon_b200_qmv_prep
  * or a fused producer wrote it).  epilogue 0: store y; epilogue 1:
- * h_out[m][n] += y[m][n] (f32) and ss_out[n/16][m] = sum of the squares of the
- * 16 updated h_out entries; epilogue 2: for n%16 < 8 (weight tiles of 8 gate
+ * h_out[m][n] += y[m][n] (f32) and ss_out[n/16][m] (rows of 32 floats) = sum
+ * of the squares of the 16 updated h_out entries; epilogue 2: for n%16 < 8 (weight tiles of 8 gate
  * rows then the 8 matching up rows), act[m][8*(n/16) + n%8] =
  * bf16(silu(y[m][n]) * y[m][n+8]), in pair order within each 8 columns when
  * act_pair_order is set; epilogue 3: atomicMax(amax[m], key(y[m][n]) << 32 |
@@ -221,16 +245,26 @@ typedef struct affon_b200_qmv_fusion {
     void *act;
     int64_t ld_act;
     unsigned long long *amax;
+    int64_t index_offset; /* epilogue 3: added to n in the key (the first row of a vocabulary shard) */
 } affon_b200_qmv_fusion;
 
 int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
                          const void *s, const void *b, void *y, const affon_b200_qmv_fusion *fusion);
 
+/* Residual add and RMSNorm for the tensor-parallel decoder, after the
+ * all-reduce of a row-parallel projection: h[m] += add[m] (f32; add may be
+ * NULL), then dst[m] = bf16(h[m] * rsqrt(mean(h[m]^2) + eps) * gamma) in the
+ * qmv's column order for `bits`.  rows <= 32, cols <= 8192, deterministic. */
+int affon_b200_resid_norm(affon_b200_ctx *ctx, float *h, int64_t ld_h, const float *add, int64_t ld_add,
+                          const void *gamma, float eps, int rows, int cols, int bits, void *dst, int64_t ld_dst);
+
 /* Grouped-query decode attention over a [batch][kv_heads][capacity][128] bf16
  * KV cache: RoPE (rotate-half pairs, tables [capacity][64]) on the queries
  * and the new key, the new key/value written at *pos, softmax over positions
  * 0..*pos, output [batch][q_heads*128] bf16.  q/k/v are columns q_offset,
- * k_offset, v_offset of the bf16 rows of qkv. */
+ * k_offset, v_offset of the bf16 rows of qkv.  A *pos outside [0, capacity)
+ * writes nothing and makes the next affon_b200_ctx_synchronize return
+ * AFFON_B200_INVALID_ARG. */
 typedef struct affon_b200_attn_desc {
     uint32_t struct_size;
     int32_t batch, q_heads, kv_heads, head_dim, capacity;
@@ -244,15 +278,59 @@ int affon_b200_decode_attention(affon_b200_ctx *ctx, const affon_b200_attn_desc 
                                 void *k_cache, void *v_cache, const float *rope_cos, const float *rope_sin,
                                 const int *pos, void *out);
 
-/* h[b][:] = f32(table[tokens[b]][:]) with ss_out[dim/16][16] partial sums of
- * squares for the first norm; also zeroes amax[0..batch). */
-int affon_b200_embed(affon_b200_ctx *ctx, const void *table, int64_t ld_table, const int *tokens, int batch, int dim,
-                     float *h, float *ss_out, unsigned long long *amax);
+/* h[b][:] = f32(table[tokens[b]][:]) with ss_out[dim/16][32] partial sums of
+ * squares for the first norm; also zeroes amax[0..batch).  batch <= 32.  A
+ * token outside [0, vocab) reads row 0 and makes the next
+ * affon_b200_ctx_synchronize return AFFON_B200_INVALID_ARG. */
+int affon_b200_embed(affon_b200_ctx *ctx, const void *table, int64_t ld_table, int64_t vocab, const int *tokens,
+                     int batch, int dim, float *h, float *ss_out, unsigned long long *amax);
 
-/* tokens[b] = argmax index held in amax[b]; history[*step][b] = tokens[b]
- * (history may be NULL); then *pos += 1 and *step += 1. */
+/* tokens[b] = argmax index held in amax[b]; history[*step % history_rows][b]
+ * = tokens[b] (history may be NULL; it keeps the last history_rows steps);
+ * then *pos += 1 and *step += 1. */
 int affon_b200_argmax_finalize(affon_b200_ctx *ctx, const unsigned long long *amax, int batch, int *tokens,
-                               int *history, int *pos, int *step);
+                               int *history, int history_rows, int *pos, int *step);
+
+/* ---------------------------------------------------------------------------
+ * Tensor parallelism (whole-model decode sharded over the GPUs of one node,
+ * one process per GPU).  No counterpart in the reference, which has no
+ * multi-device contract (docs/core/backend-support.md:82); the sharding is
+ * column-parallel QKV / gate-up / LM head and row-parallel O / down with a
+ * sum all-reduce after each row-parallel projection.  The group is an NCCL
+ * communicator attached to a context, created non-blocking: initialisation,
+ * every collective's enqueue, affon_b200_tp_synchronize and teardown are
+ * polled against a host deadline and abort the group (AFFON_B200_TIMEOUT)
+ * instead of hanging on a peer that died or never joined.  Collectives run on
+ * the context's stream and can be captured in CUDA graphs. */
+
+#define AFFON_B200_TP_ID_BYTES 144
+
+typedef enum affon_b200_reduce_op {
+    AFFON_B200_REDUCE_SUM = 0,
+    AFFON_B200_REDUCE_MAX = 1
+} affon_b200_reduce_op;
+
+/* A sealed group id (magic, NCCL unique id, checksum) for rank 0 to share
+ * with the other ranks out of band (AFFON_B200_TP_ID_BYTES bytes). */
+int affon_b200_tp_unique_id(void *id_out);
+/* AFFON_B200_OK if `id` is an intact sealed id, else AFFON_B200_INVALID_ARG. */
+int affon_b200_tp_id_check(const void *id);
+/* Join the group as `rank` of `world` on the context's device; every rank
+ * calls it with the same id.  Waits at most timeout_s for all ranks. */
+int affon_b200_tp_init(affon_b200_ctx *ctx, int rank, int world, const void *id, double timeout_s);
+int affon_b200_tp_rank(const affon_b200_ctx *ctx);   /* -1 without a group */
+int affon_b200_tp_world(const affon_b200_ctx *ctx);  /* 0 without a group */
+/* In-place all-reduce of `count` elements on the context's stream: f32 or
+ * bf16 sum, or u64 max. */
+int affon_b200_tp_allreduce(affon_b200_ctx *ctx, void *buf, size_t count, int dtype, int op);
+int affon_b200_tp_allreduce_bf16(affon_b200_ctx *ctx, void *buf, size_t count);
+/* Wait (at most timeout_s; <= 0: the group's) for the context's stream, then
+ * report device-side failures like affon_b200_ctx_synchronize. */
+int affon_b200_tp_synchronize(affon_b200_ctx *ctx, double timeout_s);
+/* Abort the group: peers' pending and future collectives fail. */
+int affon_b200_tp_abort(affon_b200_ctx *ctx);
+/* Leave the group (bounded finalize, then destroy; abort on timeout). */
+int affon_b200_tp_destroy(affon_b200_ctx *ctx);
 
 /* Number of kernel launches this library issued in this process (all
  * contexts); lets callers and benchmarks count native launches. */

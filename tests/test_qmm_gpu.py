@@ -106,7 +106,7 @@ def _oracle_rows_f64(data, rows):
 
 @pytest.mark.parametrize("N,K", BASELINE_NK)
 @pytest.mark.parametrize("bits", [4, 8])
-@pytest.mark.parametrize("M", [1, 4, 8, 16])
+@pytest.mark.parametrize("M", [1, 4, 8, 16, 32])
 def test_qmv_baseline_shapes(ctx, M, bits, N, K):
     """BASELINE decode sweep (config 2) on seeded inputs vs the oracle.
 
@@ -138,12 +138,39 @@ def test_split_k_is_deterministic(ctx):
     assert torch.equal(y1, y2)
 
 
-@pytest.mark.parametrize("M", [17, 33, 64])
+@pytest.mark.parametrize("M", [17, 33, 64, 100])
 def test_qmv_multi_pass(ctx, M):
     data = synthetic.quantized_linear(M, 1024, 4096, bits=4, seed=5)
     y, sel = _run_dense(ctx, data, _upload(ctx, data))
     assert "qmv" in sel.implementation_id.decode()
     ref = _oracle_rows_f64(data, np.arange(1024))
+    assert np.abs(y.cpu().numpy() - ref).max() <= 1e-5 * max(1, np.abs(ref).max())
+
+
+@pytest.mark.parametrize("bits,K", [(4, 1792), (4, 3584), (8, 1920)])
+def test_qmv_k_not_multiple_of_512_with_padded_parameter_rows(ctx, bits, K):
+    """Tensor-parallel shards split K at 64-group boundaries (e.g. 14336/8 =
+    1792): K need only be a multiple of one 128-byte packed stage, with the
+    scale and bias rows padded to a 16-byte stride (a strided view)."""
+    M, N = 16, 2048
+    data = synthetic.quantized_linear(M, N, K, bits=bits, seed=12)
+    bufs = _upload(ctx, data)
+    G = K // 64
+    Gp = (G + 7) // 8 * 8
+    pad = {}
+    for k in ("s", "b"):
+        t = torch.zeros((N, Gp), dtype=torch.int16, device=ctx.device)
+        t[:, :G] = bufs[k]
+        pad[k] = t
+    d = dense_desc(M, N, K, bits)
+    d.s = _lib.View(N, G, Gp, 1, 0)
+    d.b = _lib.View(N, G, Gp, 1, 0)
+    y = torch.empty((M, N), dtype=torch.float32, device=ctx.device)
+    sel = ctx.qmm(d, bufs["x"].data_ptr(), bufs["w"].data_ptr(), pad["s"].data_ptr(), pad["b"].data_ptr(),
+                  y.data_ptr())
+    torch.cuda.synchronize()
+    assert "qmv" in sel.implementation_id.decode(), sel.reason
+    ref = _oracle_rows_f64(data, np.arange(N))
     assert np.abs(y.cpu().numpy() - ref).max() <= 1e-5 * max(1, np.abs(ref).max())
 
 

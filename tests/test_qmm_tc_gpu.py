@@ -79,6 +79,22 @@ def test_qmm_tc_baseline_distributions(ctx, bits, M, N, K):
     assert (np.abs(y32[:, rows] - ref) <= 2.0 ** -8 * mag + 1e-6).all()
 
 
+@pytest.mark.parametrize("N", [4096, 14336])
+def test_qmm_tc_m8192(ctx, N):
+    """BASELINE config 3 at its largest M (8192 rows, 4-bit, K=4096): 256
+    sampled weight rows against float64, bf16 gate 2e-2, and every output
+    finite."""
+    M, K = 8192, 4096
+    data = synthetic.quantized_linear(M, N, K, bits=4, seed=3)
+    y, impl = _run(ctx, data, "bf16")
+    assert "qmm_tcgen05" in impl, impl
+    assert np.isfinite(y).all()
+    rows = np.linspace(0, N - 1, 256).astype(np.int64)
+    ref, _ = _f64(data, rows)
+    peak = max(1.0, np.abs(ref).max())
+    assert np.abs(y[:, rows] - ref).max() / peak <= 2e-2
+
+
 def test_qmm_tc_large_property(ctx):
     """BASELINE qmm shape M=2048, N=128256, K=4096 (4-bit): sampled rows and
     columns against float64, and a checksum of checksums over all outputs."""

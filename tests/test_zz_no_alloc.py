@@ -1,13 +1,16 @@
 """The allocation-free decode qmv entry point, affon_b200_qmv_noalloc.
 
-It exists for callers that may not allocate device memory through a library
-(an arena-owning runtime, a plugin host with its own allocator, code running
-under stream capture): it needs no context and keeps its scratch in a static
-device array.  These tests call it through the C ABI and compare it with the
-regular context-based entry point on the same inputs, twice in a row (the
-array keeps the previous call's contents, so the second call checks that
-what must start at zero is cleared).  The file sorts last so that a run
-stopping at the first failure has already run every other test.
+It exists for callers that may not let a library allocate device memory (a
+runtime that owns every byte of the GPU in its own arena, a plugin host whose
+allocator alone may call the driver): it needs no context and keeps its
+scratch in a static device array.  These tests call it through the C ABI and
+compare it with the regular context-based entry point on the same inputs,
+twice in a row (the array keeps the previous call's contents, so the second
+call checks that what must start at zero is cleared).  Both run the same
+kernel with the same plan, so the results must be bit-identical; the status
+word, read back with affon_b200_qmv_noalloc_status, must say that no bounded
+wait gave up.  The file sorts last so that a run stopping at the first
+failure has already run every other test.
 """
 import ctypes
 
@@ -34,7 +37,8 @@ def _upload(data, dev):
 
 
 @pytest.mark.parametrize("M,N,K,bits,yd", [(16, 4096, 4096, 4, "f32"), (1, 14336, 4096, 4, "bf16"),
-                                           (8, 4096, 14336, 8, "f32"), (4, 28672, 4096, 4, "f32")])
+                                           (8, 4096, 14336, 8, "f32"), (4, 28672, 4096, 4, "f32"),
+                                           (32, 4096, 4096, 4, "f32")])
 def test_noalloc_matches_context_entry_twice(ctx, M, N, K, bits, yd):
     data = synthetic.quantized_linear(M, N, K, bits=bits, seed=21)
     dev = ctx.device
@@ -47,18 +51,17 @@ def test_noalloc_matches_context_entry_twice(ctx, M, N, K, bits, yd):
     sel = ctx.qmm(d, *ptrs, y_ref.data_ptr())
     assert "qmv" in sel.implementation_id.decode()
     torch.cuda.synchronize()
-    ref = y_ref.float().cpu().numpy()
-    tol = (1e-5 if yd == "f32" else 2e-2) * max(1.0, float(np.abs(ref).max()))
+    assert torch.isfinite(y_ref.float()).all()
 
     stream = torch.cuda.current_stream(dev).cuda_stream
     for _ in range(2):
         y = torch.full((M, N), float("nan"), dtype=tdt, device=dev)
         rc = _lib.lib().affon_b200_qmv_noalloc(ctypes.byref(d), *ptrs, y.data_ptr(), stream)
         assert rc == 0, _lib.last_error()
-        torch.cuda.synchronize()
-        got = y.float().cpu().numpy()
-        assert np.isfinite(got).all()
-        assert np.abs(got - ref).max() <= tol
+        status = ctypes.c_uint32(7)
+        assert _lib.lib().affon_b200_qmv_noalloc_status(stream, ctypes.byref(status)) == 0, _lib.last_error()
+        assert status.value == 0
+        assert torch.equal(y, y_ref)
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(ctx):
