@@ -24,6 +24,13 @@ AFB_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
     return r;
 }
 
+// (x0, x1) as bf16 pairs hi = bf16(x) and lo = bf16(x - hi): hi + lo carries
+// ~16 significant bits of x.
+AFB_DEVICE void split_bf16x2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    hi = pack_bf16x2(x0, x1);
+    lo = pack_bf16x2(x0 - __uint_as_float(hi << 16), x1 - __uint_as_float(hi & 0xFFFF0000u));
+}
+
 // d = (a & b) | c
 AFB_DEVICE uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;

@@ -16,7 +16,9 @@
 // bf16) and K fragments read with ldmatrix; an online softmax per warp in f32
 // (exp2); the probabilities, rounded to bf16, go from the S accumulators
 // straight into the A operand of O += P V, with V fragments from
-// ldmatrix.trans.  The warps' (max, sum, O) are merged in shared memory; when
+// ldmatrix.trans.  Q and P enter the tensor cores as bf16 hi + lo pairs (the
+// lo halves in the A rows 8..15 the at most 8 heads leave free), so the
+// products keep ~16 significant bits; the cache and q/k/v are bf16.  The warps' (max, sum, O) are merged in shared memory; when
 // the context is split over several CTAs, each writes its record and the last
 // CTA of the (batch, KV head) pair -- an arrival counter, nobody waits --
 // merges the records in split order, so the result does not depend on
@@ -71,7 +73,7 @@ __device__ __forceinline__ int out_column(int d, int pair_order) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_constant__ CUtensorMap kmap,
+__global__ void __launch_bounds__(THREADS, 2) decode_attention_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                    const __grid_constant__ CUtensorMap vmap,
                                                                    AttnParams p) {
     extern __shared__ char smem_raw[];
@@ -136,10 +138,13 @@ __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_
 
     // ------------------------------------------------------------ consumers
     const int g = lane >> 2, t = lane & 3;
-    // Q fragments: A rows = query heads (rows g < G; rows g + 8 stay zero),
-    // k-step ks covers dims 16 ks .. 16 ks + 15: a0 = dims 16ks+2t..+1,
-    // a2 = dims 16ks+2t+8..+9.  RoPE pairs (d, d + 64).
-    uint32_t qa[8][2];
+    // Q fragments.  A rows 0..7 hold the query heads (rows g < G) rounded to
+    // bf16, rows 8..15 the rounding remainders of the same heads, so one
+    // m16n8k16 gives both halves of each score (C rows g and g + 8) and the
+    // scores carry ~16 significant bits of the rotated f32 query.  k-step ks
+    // covers dims 16 ks .. 16 ks + 15: a0/a1 = dims 16ks+2t..+1 (hi/lo),
+    // a2/a3 = dims 16ks+2t+8..+9.  RoPE pairs (d, d + 64).
+    uint32_t qa[8][4];
     {
         const float qs = p.scale * LOG2E;
         const uint16_t *qrow = p.qkv + b * p.ld_qkv + p.q_off + (kvh * G + (g < G ? g : 0)) * HD;
@@ -148,13 +153,13 @@ __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_
         auto rot = [&](int d) {
             const int dd = d & 63;
             const float a = bf16_bits_to_f32(qrow[dd]), c = bf16_bits_to_f32(qrow[dd + 64]);
-            return (d < 64 ? a * cs[dd] - c * sn[dd] : c * cs[dd] + a * sn[dd]) * qs;
+            return g < G ? (d < 64 ? a * cs[dd] - c * sn[dd] : c * cs[dd] + a * sn[dd]) * qs : 0.0f;
         };
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
             const int d0 = 16 * ks + 2 * t;
-            qa[ks][0] = g < G ? pack_bf16x2(rot(d0), rot(d0 + 1)) : 0u;
-            qa[ks][1] = g < G ? pack_bf16x2(rot(d0 + 8), rot(d0 + 9)) : 0u;
+            split_bf16x2(rot(d0), rot(d0 + 1), qa[ks][0], qa[ks][1]);
+            split_bf16x2(rot(d0 + 8), rot(d0 + 9), qa[ks][2], qa[ks][3]);
         }
     }
     float m_run = -INFINITY, l_run = 0.0f;  // row g: running max (log2 units) and this thread's share of the sum
@@ -208,15 +213,13 @@ __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_
                 const int c = 32 * kp + 8 * (lane >> 3);  // first dim of this lane's 8x8 matrix
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(kbase + (c >> 6) * BOX + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4), b0, b1, b2, b3);
-                const uint32_t a0[4] = {qa[2 * kp][0], 0u, qa[2 * kp][1], 0u};
-                const uint32_t a1[4] = {qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u};
-                mma_bf16_16816(sc[j], a0, b0, b1, sc[j]);
-                mma_bf16_16816(sc[j], a1, b2, b3, sc[j]);
+                mma_bf16_16816(sc[j], qa[2 * kp], b0, b1, sc[j]);
+                mma_bf16_16816(sc[j], qa[2 * kp + 1], b2, b3, sc[j]);
             }
         }
         // Online softmax of row g over the 4 scores this thread holds.
         const int p0 = i * TILE + warp * 16 + 2 * t;
-        float v[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
+        float v[4] = {sc[0][0] + sc[0][2], sc[0][1] + sc[0][3], sc[1][0] + sc[1][2], sc[1][1] + sc[1][3]};
         const int pp[4] = {p0, p0 + 1, p0 + 8, p0 + 9};
         float mx = -INFINITY;
 #pragma unroll
@@ -237,9 +240,15 @@ __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_
         for (int n = 0; n < 16; ++n) {
             o[n][0] *= corr;
             o[n][1] *= corr;
+            o[n][2] *= corr;
+            o[n][3] *= corr;
         }
-        // O += P V: P is the A operand (row g, positions 2t..2t+1 and 2t+8..+9).
-        const uint32_t pa[4] = {pack_bf16x2(pr[0], pr[1]), 0u, pack_bf16x2(pr[2], pr[3]), 0u};
+        // O += P V: P is the A operand, hi in rows g (positions 2t..2t+1 and
+        // 2t+8..+9) and the remainders in rows g + 8, like Q; the two halves
+        // of O are added at the end.
+        uint32_t pa[4];
+        split_bf16x2(pr[0], pr[1], pa[0], pa[1]);
+        split_bf16x2(pr[2], pr[3], pa[2], pa[3]);
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {  // dims 16jj .. 16jj+15 = n-tiles 2jj, 2jj+1
             const int mtx = lane >> 3;
@@ -267,8 +276,8 @@ __global__ void __launch_bounds__(THREADS) decode_attention_kernel(const __grid_
         }
 #pragma unroll
         for (int n = 0; n < 16; ++n) {
-            red_o[(warp * 8 + g) * HD + 8 * n + 2 * t] = o[n][0];
-            red_o[(warp * 8 + g) * HD + 8 * n + 2 * t + 1] = o[n][1];
+            red_o[(warp * 8 + g) * HD + 8 * n + 2 * t] = o[n][0] + o[n][2];
+            red_o[(warp * 8 + g) * HD + 8 * n + 2 * t + 1] = o[n][1] + o[n][3];
         }
     }
     named_bar_sync(1, CT);

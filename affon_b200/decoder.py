@@ -30,10 +30,11 @@ the winner, so every rank samples the same tokens.
 
 A decode step is captured once in a CUDA graph: the current position,
 step counter and tokens live in device memory and are advanced by the last
-kernel, so replays run back to back with no host work.  The decoder's context
-runs in overlap mode (programmatic dependent launch): each kernel of the step
-starts while the previous one finishes and streams its weights ahead of the
-activations it waits for.
+kernel, so replays run back to back with no host work.  `overlap=True` runs
+the context in overlap mode (programmatic dependent launch: each kernel of
+the step may start while the previous one finishes and stream its weights
+ahead of the activations it waits for); it is off by default because the
+captured 8B step measured slower with it (5.34 vs 4.61 ms).
 """
 import ctypes
 import math
@@ -155,7 +156,7 @@ class QuantizedDecoder:
     rank's shard of a tensor-parallel decoder (group_id from
     affon_b200.tp.unique_id on rank 0, shared with every rank)."""
 
-    def __init__(self, cfg, batch, capacity, device, seed=0, max_steps=4096, workspace_bytes=None, overlap=True,
+    def __init__(self, cfg, batch, capacity, device, seed=0, max_steps=4096, workspace_bytes=None, overlap=False,
                  tp=None):
         if batch > _lib.MAX_QMV_ROWS:
             raise ValueError(f"decode qmv handles up to {_lib.MAX_QMV_ROWS} rows per step")
@@ -215,7 +216,7 @@ class QuantizedDecoder:
         check(L.affon_b200_ctx_create(dev.index, None, ctypes.byref(self.ctx)), "decoder context")
         if workspace_bytes:
             check(L.affon_b200_ctx_reserve_workspace(self.ctx, int(workspace_bytes)))
-        # The step's kernels never write weights, so they may overlap.
+        # The step's kernels never write weights, so overlap mode is safe here.
         self._overlap = overlap
         check(L.affon_b200_ctx_set_overlap(self.ctx, 1 if overlap else 0))
         self.tp = None

@@ -86,7 +86,8 @@ def add(a, b):
     if isinstance(a, FormalTensor) != isinstance(b, FormalTensor):
         raise TypeError("add cannot mix formal and evaluated tensors")
     if isinstance(a, FormalTensor):
-        if a.spec.shape != b.spec.shape or a.spec.dtype != b.spec.dtype:
+        # Same shapes, or b a vector over a's last axis (a layer bias).
+        if a.spec.dtype != b.spec.dtype or (a.spec.shape != b.spec.shape and b.spec.shape != a.spec.shape[-1:]):
             raise TypeError("add requires matching shapes and dtypes")
         return a.program.emit("add", [a, b], a.spec)
     return _immediate("add", [a, b], lambda v: add(*v))

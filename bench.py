@@ -394,7 +394,10 @@ def run_decode(args, rank, world, dev):
     prompt = torch.randint(0, cfg.vocab, (ctxlen, B), generator=gen)
     dec.capture()
     t0 = time.time()
-    dec.prefill(prompt)                     # positions 0..1023 through the same graph
+    if args.kv == "prefill":
+        dec.prefill(prompt)                 # positions 0..1023 through the same graph
+    else:
+        dec.fill_kv_random(ctxlen)          # same step cost, no teacher-forced steps
     dec.synchronize(120.0)
     prefill_s = time.time() - t0
     dec.reset(ctxlen)
@@ -455,9 +458,10 @@ def run_decode(args, rank, world, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    # The same timed replays with programmatic dependent launch off (graph
-    # recaptured), to show what the overlap between kernels buys.
-    check(L.affon_b200_ctx_set_overlap(dec.ctx, 0))
+    # The same timed replays with programmatic dependent launch on (graph
+    # recaptured), to show what overlapping the step's kernels does.
+    check(L.affon_b200_ctx_set_overlap(dec.ctx, 1))
+    dec._overlap = True
     dec.capture()
     dec.reset(pos0)
     for _ in range(2):
@@ -469,12 +473,13 @@ def run_decode(args, rank, world, dev):
         dec.replay()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    off_ms = e0.elapsed_time(e1) / args.steps
+    on_ms = e0.elapsed_time(e1) / args.steps
     if world > 1:
-        t = torch.tensor([off_ms], device=dev)
+        t = torch.tensor([on_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        off_ms = float(t.item())
-    check(L.affon_b200_ctx_set_overlap(dec.ctx, 1))
+        on_ms = float(t.item())
+    check(L.affon_b200_ctx_set_overlap(dec.ctx, 0))
+    dec._overlap = False
     dec.capture()
     dec.reset(pos0 + args.steps)
 
@@ -512,7 +517,9 @@ def run_decode(args, rank, world, dev):
         "dtype": "u4 codes x bf16 -> f32 accumulate, bf16 activations",
         "config": {"workload": "decode_llama3_8b_b16_ctx1024", "model": "llama3-8b-shape (random init, 4-bit g64)",
                    "global_batch": B, "seq_len": ctxlen, "layers": cfg.layers, "d_model": cfg.d_model,
-                   "ffn": cfg.ffn, "vocab": cfg.vocab, "kv_cache": "prefilled by 1024 teacher-forced decode steps",
+                   "ffn": cfg.ffn, "vocab": cfg.vocab,
+                   "kv_cache": "prefilled by 1024 teacher-forced decode steps" if args.kv == "prefill" else
+                   "1024 positions of random bf16 values",
                    "prefill_seconds": round(prefill_s, 2), "l2": "weights 4.2 GB >> L2 (no L2 flush needed)",
                    "step_hbm_bytes": step_bytes, "weight_bytes": wbytes,
                    "roofline_tok_s_weights_plus_kv": round(roof_tok_s, 1),
@@ -520,8 +527,7 @@ def run_decode(args, rank, world, dev):
                    "roofline_tok_s_weights_only": round(roof_w_tok_s, 1),
                    "frac_of_weights_only_roofline": round(tok_s / roof_w_tok_s, 4),
                    "step_achieved_gbs": round(step_bytes / (ms_max * 1e-3) / 1e9, 1),
-                   "overlap": "programmatic dependent launch between the step's kernels",
-                   "ms_per_step_overlap_off": round(off_ms, 4)},
+                   "ms_per_step_overlap_on": round(on_ms, 4)},
         "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 4,
                 "d2h_bytes_per_step": B * 4, "ms_per_step": round(e2e_ms, 4),
                 "path": "decoder graph replay with pinned token H2D/D2H and host read each step"},
@@ -612,6 +618,161 @@ def run_config5(args, rank, world, dev):
         torch.cuda.empty_cache()
 
 
+KERNEL_CASES = {
+    # name: (M, N, K, bits, epilogue) -- decoder projections of the 8B shape at batch 16
+    "gate_up": (16, 28672, 4096, 4, "silu"), "down": (16, 4096, 14336, 4, "resid"),
+    "qkv": (16, 6144, 4096, 4, "store"), "o": (16, 4096, 4096, 4, "resid"),
+    "lm_head": (16, 128256, 4096, 4, "store"), "lm_head_m1": (1, 128256, 4096, 4, "store"),
+    "qmv_m32": (32, 28672, 4096, 4, "store"),
+}
+
+
+def _timed_launches(launch, warmup, steps, dev):
+    """Average device time (ms) of `steps` launches after `warmup`, CUDA events
+    on the current stream."""
+    import torch
+    for _ in range(warmup):
+        launch()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / steps
+
+
+def run_kernel(args, dev):
+    """One hot kernel alone, `steps` launches after `warmup`, on a bounded case
+    whose operands exceed L2 (weights or caches rotated over enough copies):
+    the command the ncu captures under profiles/ run.  Prints one JSON line
+    with the average launch time and the achieved throughput."""
+    import ctypes
+    import torch
+    from affon_b200 import _lib
+    from affon_b200.core import check
+    L = _lib.lib()
+    pk, _ = peaks()
+    if args.kernel == "attn":
+        from affon_b200.decoder import LlamaConfig, QuantizedDecoder
+        cfg = LlamaConfig(layers=4, d_model=4096, q_heads=32, kv_heads=8, head_dim=128, ffn=512, vocab=512)
+        dec = QuantizedDecoder(cfg, 16, 1088, dev, seed=0, max_steps=8)
+        dec.fill_kv_random(1024)
+        idx = [0]
+
+        def launch():
+            kc, vc = dec._kv_layer[idx[0] % cfg.layers]
+            idx[0] += 1
+            check(L.affon_b200_decode_attention(dec.ctx, ctypes.byref(dec.attn_desc), dec.qkv.data_ptr(),
+                                                kc.data_ptr(), vc.data_ptr(), dec.cos.data_ptr(), dec.sin.data_ptr(),
+                                                dec.pos.data_ptr(), dec.attn.data_ptr()))
+        dec.set_stream(torch.cuda.current_stream(dev))
+        ms = _timed_launches(launch, args.warmup, args.steps, dev)
+        nbytes = 2 * 16 * 8 * 1025 * 128 * 2
+        dec.close()
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"kernel": "attn", "case": "B=16 kvh=8 G=4 ctx=1025, 4 layer caches rotated (286 MB)",
+                          "us_per_launch": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                          "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 4), "bytes_per_launch": nbytes}))
+        return 0
+    ctx = ctypes.c_void_p()
+    check(L.affon_b200_ctx_create(dev.index, None, ctypes.byref(ctx)))
+    check(L.affon_b200_ctx_set_stream(ctx, torch.cuda.current_stream(dev).cuda_stream))
+    try:
+        if args.kernel == "qmm":
+            M, N, K, bits = 2048, 4096, 4096, 4
+            _, sets = make_qmv_operands(dev, 1, N, K, bits, 64, copies=1, seed=4)
+            w, sc, b = sets[0]
+            xm = torch.randn((M, K), device=dev).to(torch.bfloat16)
+            y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            d = _qmm_desc(M, N, K, bits, 64, "bf16")
+            ms = _timed_launches(lambda: check(L.affon_b200_qmm(ctx, ctypes.byref(d), xm.data_ptr(), w.data_ptr(),
+                                                                sc.data_ptr(), b.data_ptr(), y.data_ptr())),
+                                 args.warmup, args.steps, dev)
+            tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            print(json.dumps({"kernel": "qmm", "case": f"M={M} N={N} K={K} 4-bit, bf16 result",
+                              "ms_per_launch": round(ms, 4), "TFLOP/s": round(tf, 1),
+                              "frac_of_measured_bf16": round(tf / pk["bf16_tflops"], 4)}))
+            return 0
+        M, N, K, bits, epi = KERNEL_CASES[args.kernel]
+        wbytes = N * K * bits // 8 + N * (K // 64) * 4
+        copies = max(2, -(-260_000_000 // wbytes))
+        x, sets = make_qmv_operands(dev, M, N, K, bits, 64, copies)
+        d = _qmm_desc(M, N, K, bits, 64, "bf16")
+        h = torch.zeros((M, N), dtype=torch.float32, device=dev)
+        ss = torch.zeros((max(1, N // 16), 32), dtype=torch.float32, device=dev)
+        act = torch.zeros((M, N // 2), dtype=torch.bfloat16, device=dev)
+        y = torch.zeros((M, N), dtype=torch.bfloat16, device=dev)
+        fz = _lib.QmvFusion(struct_size=ctypes.sizeof(_lib.QmvFusion), x_mode=1)
+        if epi == "silu":
+            fz.epilogue, fz.act, fz.ld_act, fz.act_pair_order = _lib.EPI_SILU_MUL, act.data_ptr(), N // 2, 1
+        elif epi == "resid":
+            fz.epilogue, fz.h_out, fz.ld_h_out, fz.ss_out = _lib.EPI_RESID, h.data_ptr(), N, ss.data_ptr()
+        idx = [0]
+
+        def launch():
+            w, sc, b = sets[idx[0] % copies]
+            idx[0] += 1
+            check(L.affon_b200_qmv_fused(ctx, ctypes.byref(d), x.data_ptr(), w.data_ptr(), sc.data_ptr(),
+                                         b.data_ptr(), y.data_ptr(), ctypes.byref(fz)))
+        ms = _timed_launches(launch, args.warmup, args.steps, dev)
+        nbytes = qmv_bytes(M, N, K, bits, 64, 2)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"kernel": args.kernel, "case": f"M={M} N={N} K={K} {bits}-bit g64, {epi} epilogue, "
+                          f"{copies} weight copies rotated ({copies * wbytes / 1e6:.0f} MB)",
+                          "us_per_launch": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                          "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 4), "bytes_per_launch": nbytes}))
+        return 0
+    finally:
+        L.affon_b200_ctx_destroy(ctx)
+
+
+def run_sweep(args, dev):
+    """the decode qmv over M x bits x (N, K), through the
+    public affon_b200_qmm entry (f32 result), each point a CUDA graph of
+    back-to-back launches rotating over weight copies larger than L2.  One
+    JSON line per point."""
+    import ctypes
+    import torch
+    from affon_b200 import _lib
+    from affon_b200.core import check
+    L = _lib.lib()
+    pk, _ = peaks()
+    ctx = ctypes.c_void_p()
+    check(L.affon_b200_ctx_create(dev.index, None, ctypes.byref(ctx)))
+    shapes = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+    try:
+        for bits in (4, 8):
+            for (N, K) in shapes:
+                wbytes = N * K * bits // 8 + N * (K // 64) * 4
+                copies = max(2, -(-260_000_000 // wbytes))
+                x, sets = make_qmv_operands(dev, 32, N, K, bits, 64, copies)
+                for M in (1, 4, 8, 16, 32):
+                    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+                    d = _qmm_desc(M, N, K, bits, 64, "f32")
+                    sel = _lib.Selection()
+                    check(L.affon_b200_select(ctypes.byref(d), ctypes.byref(sel)))
+                    idx = [0]
+
+                    def launch(s, d=d, y=y):
+                        w, sc, b = sets[idx[0] % copies]
+                        idx[0] += 1
+                        check(L.affon_b200_ctx_set_stream(ctx, s.cuda_stream))
+                        check(L.affon_b200_qmm(ctx, ctypes.byref(d), x.data_ptr(), w.data_ptr(), sc.data_ptr(),
+                                               b.data_ptr(), y.data_ptr()))
+                    ms = _graph_time_ms(launch, 20, dev)
+                    nbytes = qmv_bytes(M, N, K, bits, 64, 4)
+                    gbs = nbytes / (ms * 1e-3) / 1e9
+                    print(json.dumps({"M": M, "N": N, "K": K, "bits": bits, "us": round(ms * 1e3, 2),
+                                      "GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / pk["hbm_gbs"], 4),
+                                      "impl": sel.implementation_id.decode(), "splits": sel.splits}), flush=True)
+                del x, sets
+    finally:
+        L.affon_b200_ctx_destroy(ctx)
+    return 0
+
+
 def cpu_baseline_decode(args, threads, seconds_target=15.0):
     """CPU oracle on a bounded sample of the decode step: M=16 rows through
     a slice of a K=4096 projection, scaled to the whole step's weights.
@@ -693,6 +854,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-keys", action="store_true", help="skip the stand-alone qmv/qmm kernel figures")
     ap.add_argument("--no-config5", action="store_true", help="skip the 70B (BASELINE config 5) extra key")
+    ap.add_argument("--kv", default="prefill", choices=["prefill", "random"],
+                    help="fill the 1024-position KV cache by teacher-forced decode steps (default) or with random "
+                         "values (same step cost; used for profiler runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
