@@ -33,7 +33,9 @@ class QmmDesc(ctypes.Structure):
 class QmvFusion(ctypes.Structure):
     _fields_ = [("struct_size", c_u32), ("x_mode", c_i32), ("epilogue", c_i32), ("act_pair_order", c_i32),
                 ("h_out", c_vp), ("ld_h_out", c_i64), ("ss_out", c_vp), ("act", c_vp), ("ld_act", c_i64),
-                ("amax", c_vp), ("index_offset", c_i64)]
+                ("amax", c_vp), ("index_offset", c_i64), ("row_ss", c_vp), ("ss_tiles", c_i32),
+                ("eps", ctypes.c_float), ("next_gamma", c_vp), ("next_x", c_vp), ("ld_next_x", c_i64),
+                ("next_pair_order", c_i32), ("exchange_region", c_i32)]
 
 
 class AttnDesc(ctypes.Structure):
@@ -43,7 +45,7 @@ class AttnDesc(ctypes.Structure):
                 ("ld_out", c_i64)]
 
 
-EPI_STORE, EPI_RESID, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
+EPI_STORE, EPI_RESID, EPI_SILU_MUL, EPI_ARGMAX, EPI_RESID_AR = 0, 1, 2, 3, 4
 SS_WIDTH = 32      # row width of the per-16-column sums of squares ([cols/16][SS_WIDTH] f32)
 MAX_QMV_ROWS = 32  # activation rows the decode qmv takes in one pass
 
@@ -84,6 +86,7 @@ SIGNATURES = {
     "affon_b200_tp_unique_id": ([c_vp], c_i32),
     "affon_b200_tp_id_check": ([c_vp], c_i32),
     "affon_b200_tp_init": ([c_vp, c_i32, c_i32, c_vp, ctypes.c_double], c_i32),
+    "affon_b200_tp_exchange_reserve": ([c_vp, c_i32, c_i64], c_i32),
     "affon_b200_tp_rank": ([c_vp], c_i32),
     "affon_b200_tp_world": ([c_vp], c_i32),
     "affon_b200_tp_allreduce": ([c_vp, c_vp, c_sz, c_i32, c_i32], c_i32),
@@ -92,7 +95,8 @@ SIGNATURES = {
     "affon_b200_tp_abort": ([c_vp], c_i32),
     "affon_b200_tp_destroy": ([c_vp], c_i32),
     "affon_b200_decode_attention": ([c_vp, ctypes.POINTER(AttnDesc), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
-    "affon_b200_embed": ([c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp], c_i32),
+    "affon_b200_embed": ([c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32],
+                         c_i32),
     "affon_b200_argmax_finalize": ([c_vp, c_vp, c_i32, c_vp, c_vp, c_i32, c_vp, c_vp], c_i32),
     "affon_b200_launch_count": ([], ctypes.c_uint64),
 }

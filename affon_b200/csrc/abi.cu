@@ -471,9 +471,20 @@ int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, c
     f.act_pair_order = fusion->act_pair_order;
     f.amax = fusion->amax;
     f.index_offset = fusion->index_offset;
+    f.row_ss = fusion->row_ss;
+    f.ss_tiles = fusion->ss_tiles;
+    f.eps = fusion->eps;
+    f.next_gamma = static_cast<const uint16_t *>(fusion->next_gamma);
+    f.next_x = static_cast<uint16_t *>(fusion->next_x);
+    f.ld_next_x = fusion->ld_next_x;
+    f.next_pair_order = fusion->next_pair_order;
+    if (f.row_ss && (f.ss_tiles <= 0 || f.ss_tiles * 16 != desc->x.cols || desc->x.rows > afb::kMaxQmvRows))
+        return fail(AFFON_B200_INVALID_ARG, "qmv_fused: row scales need ss_tiles = K / 16");
+    if (f.next_x && ((f.epi != 1 && f.epi != 4) || !f.next_gamma || f.ld_next_x < desc->w.rows))
+        return fail(AFFON_B200_INVALID_ARG, "qmv_fused: next_x needs the residual epilogue, next_gamma and ld >= N");
     if (f.x_mode != 0 && f.x_mode != 1) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: x_mode must be 0 or 1");
-    if (f.epi < 0 || f.epi > 3) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: unknown epilogue");
-    if ((f.epi == 1 && (!f.h_out || !f.ss_out)) || (f.epi == 2 && !f.act) || (f.epi == 3 && !f.amax) ||
+    if (f.epi < 0 || f.epi > 4) return fail(AFFON_B200_INVALID_ARG, "qmv_fused: unknown epilogue");
+    if (((f.epi == 1 || f.epi == 4) && (!f.h_out || !f.ss_out)) || (f.epi == 2 && !f.act) || (f.epi == 3 && !f.amax) ||
         (f.epi == 0 && !y))
         return fail(AFFON_B200_INVALID_ARG, "qmv_fused: missing epilogue buffer");
     if (f.epi == 2 && desc->w.rows % 16) return fail(AFFON_B200_INVALID_SHAPE, "qmv_fused: silu*mul needs N % 16 == 0");
@@ -484,6 +495,12 @@ int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, c
     if (!afb::qmv_supported(a, &why)) return fail(AFFON_B200_UNSUPPORTED, "qmv_fused: %s", why);
     const afb::QmvPlan plan = afb::qmv_plan(a, ctx->num_sms, ctx->workspace_bytes);
     if (plan.splits < 1) return fail(AFFON_B200_UNSUPPORTED, "qmv_fused: no plan fits the context workspace");
+    if (f.epi == 4) {
+        const int64_t units = (a.N + plan.rows - 1) / plan.rows * plan.max_slots;
+        const char *why = "";
+        if (!afb::tp_bind_exchange(ctx, fusion->exchange_region, a.M, a.N, units, &f, &why))
+            return fail(AFFON_B200_INVALID_ARG, "qmv_fused: %s", why);
+    }
     DeviceGuard guard(ctx->device);
     cudaError_t e = afb::launch_qmv(a, plan, ctx->workspace, ctx->stream, &f, ctx->overlap);
     if (e != cudaSuccess) return cuda_fail(e, "qmv_fused launch");
@@ -568,14 +585,16 @@ int affon_b200_decode_attention(affon_b200_ctx *ctx, const affon_b200_attn_desc 
 }
 
 int affon_b200_embed(affon_b200_ctx *ctx, const void *table, int64_t ld_table, int64_t vocab, const int *tokens,
-                     int batch, int dim, float *h, float *ss_out, unsigned long long *amax) {
+                     int batch, int dim, float *h, float *ss_out, unsigned long long *amax, const void *gamma,
+                     void *x, int64_t ld_x, int pair_order) {
     t_error.clear();
     if (!ctx || !table || !tokens || !h || !ss_out || !amax || batch <= 0 || batch > afb::kMaxQmvRows || dim <= 0 ||
-        dim % 16 || vocab <= 0)
+        dim % 16 || vocab <= 0 || (gamma && (!x || ld_x < dim)))
         return fail(AFFON_B200_INVALID_ARG, "embed: bad arguments (batch <= 32, dim % 16 == 0, vocab > 0)");
     DeviceGuard guard(ctx->device);
-    cudaError_t e = afb::launch_embed(table, ld_table, vocab, tokens, batch, dim, h, ss_out, amax, ctx->workspace,
-                                      ctx->stream, ctx->overlap);
+    cudaError_t e = afb::launch_embed(table, ld_table, vocab, tokens, batch, dim, h, ss_out, amax,
+                                      static_cast<const uint16_t *>(gamma), static_cast<uint16_t *>(x), ld_x,
+                                      pair_order, ctx->workspace, ctx->stream, ctx->overlap);
     if (e != cudaSuccess) return cuda_fail(e, "embed launch");
     return AFFON_B200_OK;
 }

@@ -351,7 +351,8 @@ __global__ void __launch_bounds__(THREADS, 2) decode_attention_kernel(const __gr
 // buffer.  A token outside [0, vocab) reads row 0 instead and sets the status
 // word.
 __global__ void embed_kernel(const uint16_t *table, int64_t ld_table, int64_t vocab, const int *tokens, int B, int D,
-                             float *h, float *ss_out, unsigned long long *amax, unsigned *status) {
+                             float *h, float *ss_out, unsigned long long *amax, const uint16_t *gamma, uint16_t *x,
+                             int64_t ld_x, int pair_order, unsigned *status) {
     pdl_wait();
     const int b = blockIdx.y;
     const int tile = blockIdx.x * (blockDim.x / 16) + threadIdx.x / 16;  // 16 columns per tile
@@ -366,6 +367,7 @@ __global__ void embed_kernel(const uint16_t *table, int64_t ld_table, int64_t vo
     if (col < D) {
         v = bf16_bits_to_f32(table[static_cast<int64_t>(tok) * ld_table + col]);
         h[static_cast<int64_t>(b) * D + col] = v;
+        if (gamma) x[b * ld_x + out_column(col, pair_order)] = f32_to_bf16_bits(v * bf16_bits_to_f32(gamma[col]));
     }
     float sq = v * v;
 #pragma unroll
@@ -467,13 +469,13 @@ cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, in
 }
 
 cudaError_t launch_embed(const void *table, int64_t ld_table, int64_t vocab, const int *tokens, int B, int D,
-                         float *h, float *ss_out, unsigned long long *amax, void *workspace, cudaStream_t stream,
-                         bool pdl) {
+                         float *h, float *ss_out, unsigned long long *amax, const uint16_t *gamma, uint16_t *x,
+                         int64_t ld_x, int pair_order, void *workspace, cudaStream_t stream, bool pdl) {
     const int threads = 256;  // 16 tiles of 16 columns per block
     dim3 grid((D + threads - 1) / threads, B);
     cudaError_t e = launch_ex(dec::embed_kernel, grid, dim3(threads), 0, stream, false, pdl,
                               static_cast<const uint16_t *>(table), ld_table, vocab, tokens, B, D, h, ss_out, amax,
-                              static_cast<unsigned *>(workspace));
+                              gamma, x, ld_x, pair_order, static_cast<unsigned *>(workspace));
     count_launch();
     return e;
 }

@@ -48,6 +48,9 @@ constexpr size_t kCounterOffset = 256;
 // residual epilogue writes and the RMSNorm prologue reads.
 constexpr int kMaxQmvRows = 32;
 constexpr int kSsWidth = 32;
+// Tensor-parallel exchange: ranks at most, and arrival flags per region.
+constexpr int kTpMaxWorld = 8;
+constexpr int kTpMaxUnits = 65536;
 constexpr int64_t kMaxTiles = 262144;
 constexpr size_t kPartialOffset = kCounterOffset + size_t(kMaxTiles) * 4;
 // Optional fusions of the decode qmv (decoder use).  Activations: natural
@@ -59,7 +62,10 @@ constexpr size_t kPartialOffset = kCounterOffset + size_t(kMaxTiles) * 4;
 // matching 8 up rows (optionally in the 4-bit pair order); per-row argmax
 // packed as (order-preserving key << 32 | ~n) with atomicMax (lowest index
 // wins ties).
-enum QmvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3 };
+// EPI_RESID_AR: EPI_RESID of the sum over the tensor-parallel group of
+// every rank's output (a row-parallel projection): the rows are pushed to
+// every rank's exchange buffer, and each rank sums the pushes in rank order.
+enum QmvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SILU_MUL = 2, EPI_ARGMAX = 3, EPI_RESID_AR = 4 };
 struct QmvFusion {
     int x_mode = 0;                 // 0: natural bf16 x; 1: x already in the kernel's order
     int epi = EPI_STORE;
@@ -71,6 +77,25 @@ struct QmvFusion {
     int act_pair_order = 0;         // EPI_SILU_MUL: write act in the 4-bit pair order
     unsigned long long *amax = nullptr;  // EPI_ARGMAX: [M]
     int64_t index_offset = 0;       // EPI_ARGMAX: added to the row index (a vocabulary shard's first row)
+    // Row-scale mode: x is bf16(h * gamma) (not normalised); every output of
+    // activation row m is multiplied by rsqrt(sum_k h[m][k]^2 / K + eps),
+    // with the sums of squares taken from row_ss ([ss_tiles][kSsWidth]).
+    const float *row_ss = nullptr;
+    int ss_tiles = 0;
+    float eps = 0.0f;
+    // EPI_RESID: also write next_x[m][col(n)] = bf16(h_new[m][n] * next_gamma[n])
+    // (the next projection's row-scale-mode activations; col in pair order
+    // when next_pair_order).
+    const uint16_t *next_gamma = nullptr;
+    uint16_t *next_x = nullptr;
+    int64_t ld_next_x = 0;
+    int next_pair_order = 0;
+    // EPI_RESID_AR: every rank's receive area ([world][M][N] f32) and arrival
+    // flags of this call's exchange region.
+    int tp_world = 1, tp_rank = 0;
+    float *tp_recv[kTpMaxWorld] = {};
+    unsigned *tp_flags_peer[kTpMaxWorld] = {};
+    unsigned *tp_flags_local = nullptr;
 };
 bool qmv_supported(const QmmArgs &a, const char **why);
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes);
@@ -119,8 +144,8 @@ size_t attention_workspace_bytes(int batch, int kv_heads, int q_heads, int capac
 cudaError_t launch_decode_attention(const DecodeAttnArgs &a, void *workspace, int num_sms, cudaStream_t stream,
                                     bool pdl);
 cudaError_t launch_embed(const void *table, int64_t ld_table, int64_t vocab, const int *tokens, int B, int D,
-                         float *h, float *ss_out, unsigned long long *amax, void *workspace, cudaStream_t stream,
-                         bool pdl);
+                         float *h, float *ss_out, unsigned long long *amax, const uint16_t *gamma, uint16_t *x,
+                         int64_t ld_x, int pair_order, void *workspace, cudaStream_t stream, bool pdl);
 cudaError_t launch_finalize(const unsigned long long *amax, int B, int *tokens, int *history, int history_rows,
                             int *pos, int *step, cudaStream_t stream, bool pdl);
 
@@ -156,6 +181,10 @@ struct affon_b200_ctx {
 namespace afb {
 // Tears down the context's tensor-parallel state (tp.cu).
 void tp_release(affon_b200_ctx *ctx);
+// Fill f's exchange fields for a row-parallel qmv of `rows` x `cols` outputs
+// with `units` row units, using exchange region `region` (0 or 1).
+bool tp_bind_exchange(affon_b200_ctx *ctx, int region, int64_t rows, int64_t cols, int64_t units, QmvFusion *f,
+                      const char **why);
 // Descriptor validation, argument resolution and the thread-local error
 // message of the C ABI (abi.cu), for other entry points of the library.
 int validate_qmm_desc(const affon_b200_qmm_desc *d);

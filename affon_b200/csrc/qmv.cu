@@ -170,18 +170,69 @@ __device__ __forceinline__ int pair_slot(int e) { return (e < 4) ? 2 * e : 2 * (
 // Returns the contribution of this pair to the per-tile reductions:
 // EPI_RESID: sum of squares of the updated residual entries; EPI_ARGMAX: the
 // packed best (key << 32 | ~n) of the pair.  Rows at or beyond N are skipped.
+// Residual update of one element: h += v, the next projection's
+// activation bf16(h * gamma_next) at its column-order position when asked,
+// and the square for the sums of squares.
+__device__ __forceinline__ float resid_update(const Params &p, int m, int64_t n, float v, float &ssq) {
+    float *h = p.f.h_out + m * p.f.ld_h_out;
+    const float hv = h[n] + v;
+    h[n] = hv;
+    if (p.f.next_x) {
+        const int e = static_cast<int>(n & 7);
+        const int64_t col = p.f.next_pair_order ? (n & ~int64_t(7)) + pair_slot(e) : n;
+        p.f.next_x[m * p.f.ld_next_x + col] = f32_to_bf16_bits(hv * bf16_bits_to_f32(p.f.next_gamma[n]));
+    }
+    ssq = fmaf(hv, hv, ssq);
+    return hv;
+}
+
+// EPI_RESID_AR: this rank's value of output (m, n) into every rank's receive
+// area, at this rank's slot (plain stores; the peers' areas are NVLink
+// mappings).
+__device__ __forceinline__ void ar_push(const Params &p, int m, int64_t n, float v) {
+    const int64_t off = (static_cast<int64_t>(p.f.tp_rank) * p.M + m) * p.N + n;
+#pragma unroll
+    for (int r = 0; r < kTpMaxWorld; ++r)
+        if (r < p.f.tp_world) p.f.tp_recv[r][off] = v;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *a) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// EPI_RESID_AR: after the consumer warps pushed the rows of one unit (a
+// whole block, or this CTA's share of a shared block), count the unit's
+// arrival on every rank.  Called by all consumer threads.
+template <int CW>
+__device__ __forceinline__ void ar_signal(const Params &p, int unit, int tid) {
+    __threadfence_system();
+    named_bar_sync(1, CW * 32);
+    if (tid == 0) {
+        for (int r = 0; r < p.f.tp_world; ++r) atomicAdd_system(p.f.tp_flags_peer[r] + unit, 1u);
+    }
+}
+
 __device__ __forceinline__ unsigned long long epilogue_pair(const Params &p, int m, int64_t n_lo, float v_lo,
-                                                            float v_hi, float &ssq) {
+                                                            float v_hi, float &ssq, const float *rs) {
     const int64_t n_hi = n_lo + 8;
     const bool ok_lo = n_lo < p.N, ok_hi = n_hi < p.N;
     unsigned long long best = 0ull;
+    if (rs) {  // RMSNorm scale of the (unnormalised) activation row
+        v_lo *= rs[m];
+        v_hi *= rs[m];
+    }
     switch (p.f.epi) {
     case EPI_RESID: {
-        float *h = p.f.h_out + m * p.f.ld_h_out;
-        if (ok_lo) { const float hv = h[n_lo] + v_lo; h[n_lo] = hv; ssq = fmaf(hv, hv, ssq); }
-        if (ok_hi) { const float hv = h[n_hi] + v_hi; h[n_hi] = hv; ssq = fmaf(hv, hv, ssq); }
+        if (ok_lo) resid_update(p, m, n_lo, v_lo, ssq);
+        if (ok_hi) resid_update(p, m, n_hi, v_hi, ssq);
         break;
     }
+    case EPI_RESID_AR:
+        if (ok_lo) ar_push(p, m, n_lo, v_lo);
+        if (ok_hi) ar_push(p, m, n_hi, v_hi);
+        break;
     case EPI_SILU_MUL:
         if (ok_hi) {  // tile rows 0-7 are gate rows, 8-15 the matching up rows
             // act column j = 8*(n/16) + n%8, at its pair-order slot when the
@@ -235,7 +286,8 @@ __device__ __forceinline__ void publish_tile(const Params &p, int64_t tile, int 
 // activation rows 2t, 2t+1 (+8 for the second MMA column tile).  Called by
 // all 32 lanes of the warp.
 template <int MT>
-__device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT][4], int64_t n0, int g, int t) {
+__device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT][4], int64_t n0, int g, int t,
+                                            const float *rs) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -243,7 +295,7 @@ __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT
             const int m = 2 * t + 8 * mt + h;
             float ssq = 0.0f;
             unsigned long long best = 0ull;
-            if (m < p.M) best = epilogue_pair(p, m, n0 + g, v[mt][h], v[mt][2 + h], ssq);
+            if (m < p.M) best = epilogue_pair(p, m, n0 + g, v[mt][h], v[mt][2 + h], ssq, rs);
             publish_tile(p, n0 >> 4, m, g == 0, ssq, best);
         }
 }
@@ -251,24 +303,29 @@ __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT
 // Final value v of weight row n for activation row m, one thread per row,
 // 32 consecutive rows per warp (a 16-row tile is one half warp; rows n and
 // n+8 sit in lanes l and l+8).  Called by all 32 lanes with the same m.
-__device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, float v, int lane, bool active) {
+// Residual update of rows n (one per lane, 32 consecutive rows per warp,
+// the same m) with the per-16-row sums of squares.  Called by all 32 lanes.
+__device__ __forceinline__ void resid_row(const Params &p, int m, int64_t n, float v, int lane, bool ok) {
+    float ssq = 0.0f;
+    if (ok) resid_update(p, m, n, v, ssq);
+    ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
+    ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
+    ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
+    ssq += __shfl_xor_sync(0xffffffffu, ssq, 8);
+    if (ok && (lane & 15) == 0) p.f.ss_out[(n >> 4) * kSsWidth + m] = ssq;
+}
+
+__device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, float v, int lane, bool active,
+                                           const float *rs) {
     const bool ok = active && n < p.N;
+    if (rs) v *= rs[m];
     switch (p.f.epi) {
-    case EPI_RESID: {
-        float hv = 0.0f;
-        if (ok) {
-            float *h = p.f.h_out + m * p.f.ld_h_out + n;
-            hv = *h + v;
-            *h = hv;
-        }
-        float ssq = hv * hv;
-        ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
-        ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
-        ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
-        ssq += __shfl_xor_sync(0xffffffffu, ssq, 8);
-        if (ok && (lane & 15) == 0) p.f.ss_out[(n >> 4) * kSsWidth + m] = ssq;
+    case EPI_RESID:
+        resid_row(p, m, n, v, lane, ok);
         break;
-    }
+    case EPI_RESID_AR:
+        if (ok) ar_push(p, m, n, v);
+        break;
     case EPI_SILU_MUL: {
         const float up = __shfl_down_sync(0xffffffffu, v, 8);
         if (active && (lane & 8) == 0 && n + 8 < p.N) {
@@ -310,7 +367,7 @@ __device__ __forceinline__ void block_contributors(const Params &p, int blk, int
 // written its slot.
 template <int MT, int NT, int CW>
 __device__ __forceinline__ void segment_epilogue(const Params &p, const float (&acc)[NT][MT][4], int blk, int warp,
-                                                 int g, int t, int tid) {
+                                                 int g, int t, int tid, const float *rs) {
     constexpr int CT = CW * 32;  // consumer threads
     constexpr int ROWS = 16 * NT * CW;
     int first, total;
@@ -318,7 +375,8 @@ __device__ __forceinline__ void segment_epilogue(const Params &p, const float (&
     const int64_t nb0 = static_cast<int64_t>(blk) * ROWS;
     if (total == 1) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) finish_tile<MT>(p, acc[nt], nb0 + (warp * NT + nt) * 16, g, t);
+        for (int nt = 0; nt < NT; ++nt) finish_tile<MT>(p, acc[nt], nb0 + (warp * NT + nt) * 16, g, t, rs);
+        if (p.f.epi == EPI_RESID_AR) ar_signal<CW>(p, blk * p.max_slots, tid);
         return;
     }
     const int slot = static_cast<int>(blockIdx.x) - first;
@@ -356,8 +414,8 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *a) {
 // garbage, and the counters are still reset).
 template <int ROWS, int CW>
 __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp, int lane, int tid,
-                               volatile int *abort) {
-    constexpr int CT = CW * 32, TILES = ROWS / 16, BATCH = 8;
+                               volatile int *abort, const float *rs) {
+    constexpr int CT = CW * 32, TILES = ROWS / 16, UB = 4, MAXS = 4;
     if (hi <= lo) return;
     unsigned *done = p.counters + kMaxTiles / 2;
     const int b_first = static_cast<int>(lo / p.spb), b_last = static_cast<int>((hi - 1) / p.spb);
@@ -384,28 +442,98 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
         const int t0 = slot * TILES / total, t1 = (slot + 1) * TILES / total;
         const int row0 = t0 * 16, nrows = (t1 - t0) * 16;
         const int chunks = (nrows + 31) / 32;
-        // Work unit = (32-row chunk, activation row m), one warp each.
-        for (int u = warp; u < chunks * p.M; u += CW) {
-            const int chunk = u / p.M, m = u - chunk * p.M;
-            const int rr = chunk * 32 + lane;
-            const bool active = rr < nrows;
-            const int row = row0 + (active ? rr : 0);
-            const float *src = base + static_cast<int64_t>(m) * ROWS + row;
-            const int64_t slot_stride = static_cast<int64_t>(p.M) * ROWS;
-            float v = 0.0f;
-            for (int sl0 = 0; sl0 < total; sl0 += BATCH) {
-                float tmp[BATCH];
+        const int units = chunks * p.M;
+        const int64_t slot_stride = static_cast<int64_t>(p.M) * ROWS;
+        // Work unit = (32-row chunk, activation row m), one warp each; a warp
+        // takes UB units at a time and issues every slot load of all of them
+        // before summing, so the combine costs about one L2 round trip per
+        // batch instead of one per unit.
+        for (int ub = warp; ub < units; ub += CW * UB) {
+            float part[UB][MAXS];
 #pragma unroll
-                for (int k = 0; k < BATCH; ++k) tmp[k] = __ldcg(src + min(sl0 + k, total - 1) * slot_stride);
+            for (int u = 0; u < UB; ++u) {
+                const int unit = ub + u * CW;
+                const int uu = unit < units ? unit : 0;
+                const int chunk = uu / p.M, m = uu - chunk * p.M;
+                const int rr = chunk * 32 + lane;
+                const int row = row0 + (rr < nrows ? rr : 0);
+                const float *src = base + static_cast<int64_t>(m) * ROWS + row;
 #pragma unroll
-                for (int k = 0; k < BATCH; ++k)
-                    if (sl0 + k < total) v += tmp[k];
+                for (int k = 0; k < MAXS; ++k) part[u][k] = (k < total && unit < units) ? __ldcg(src + k * slot_stride) : 0.0f;
             }
-            finish_row(p, m, static_cast<int64_t>(blk) * ROWS + row0 + rr, v, lane, active);
+            // Slots beyond MAXS (more than MAXS contributors) are added after.
+#pragma unroll
+            for (int u = 0; u < UB; ++u) {
+                const int unit = ub + u * CW;
+                if (unit >= units) break;  // warp-uniform
+                const int chunk = unit / p.M, m = unit - chunk * p.M;
+                const int rr = chunk * 32 + lane;
+                const bool active = rr < nrows;
+                const int row = row0 + (active ? rr : 0);
+                float v = 0.0f;
+#pragma unroll
+                for (int k = 0; k < MAXS; ++k)
+                    if (k < total) v += part[u][k];
+                for (int k = MAXS; k < total; ++k) v += __ldcg(base + static_cast<int64_t>(m) * ROWS + row + k * slot_stride);
+                finish_row(p, m, static_cast<int64_t>(blk) * ROWS + row0 + rr, v, lane, active, rs);
+            }
         }
+        if (p.f.epi == EPI_RESID_AR) ar_signal<CW>(p, blk * p.max_slots + slot, tid);
         if (tid == 0 && atomicAdd(&done[blk], 1u) == static_cast<unsigned>(total - 1)) {
             p.counters[blk] = 0u;
             done[blk] = 0u;
+        }
+    }
+}
+
+// EPI_RESID_AR, last phase: for every unit this CTA pushed, wait (bounded)
+// until every rank has pushed the same rows, then sum them in rank order and
+// apply the residual update.  Every rank finalises the same units with the
+// same plan, so a unit's flag reaches the world size exactly once per launch;
+// the waiter resets it.
+template <int ROWS, int CW>
+__device__ void ar_finish(const Params &p, int64_t lo, int64_t hi, int warp, int lane, int tid, volatile int *abort) {
+    constexpr int CT = CW * 32, TILES = ROWS / 16;
+    if (hi <= lo) return;
+    const int b_first = static_cast<int>(lo / p.spb), b_last = static_cast<int>((hi - 1) / p.spb);
+    for (int blk = b_first; blk <= b_last; ++blk) {
+        int first, total;
+        block_contributors(p, blk, first, total);
+        const int slot = total == 1 ? 0 : static_cast<int>(blockIdx.x) - first;
+        const int unit = blk * p.max_slots + slot;
+        if (tid == 0) {
+            const uint64_t start = globaltimer();
+            while (ld_acquire_sys(p.f.tp_flags_local + unit) < static_cast<unsigned>(p.f.tp_world)) {
+                if (*abort || globaltimer() - start > p.arrival_wait_ns) {
+                    *abort = 1;
+                    atomicExch(p.status, static_cast<unsigned>(DEV_TIMEOUT));
+                    break;
+                }
+                __nanosleep(64);
+            }
+            p.f.tp_flags_local[unit] = 0u;  // no rank touches it again in this launch
+        }
+        named_bar_sync(1, CT);
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        const int t0 = total == 1 ? 0 : slot * TILES / total, t1 = total == 1 ? TILES : (slot + 1) * TILES / total;
+        const int row0 = t0 * 16, nrows = (t1 - t0) * 16;
+        const int units = ((nrows + 31) / 32) * p.M;
+        const int64_t src_stride = static_cast<int64_t>(p.M) * p.N;
+        const float *recv = p.f.tp_recv[p.f.tp_rank];
+        for (int u = warp; u < units; u += CW) {
+            const int chunk = u / p.M, m = u - chunk * p.M;
+            const int rr = chunk * 32 + lane;
+            const int64_t n = static_cast<int64_t>(blk) * ROWS + row0 + rr;
+            const bool ok = rr < nrows && n < p.N;
+            float part[kTpMaxWorld];
+#pragma unroll
+            for (int r = 0; r < kTpMaxWorld; ++r)
+                part[r] = (ok && r < p.f.tp_world) ? __ldcg(recv + r * src_stride + static_cast<int64_t>(m) * p.N + n) : 0.0f;
+            float v = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kTpMaxWorld; ++r)
+                if (r < p.f.tp_world) v += part[r];
+            resid_row(p, m, n, v, lane, ok);
         }
     }
 }
@@ -425,6 +553,8 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
     uint64_t *empty = full + MAX_STAGES;
     uint64_t *xsfull = empty + MAX_STAGES;
     volatile int *abort = reinterpret_cast<volatile int *>(xsfull + MAX_STAGES);
+    __shared__ float s_rscale[MAX_XR];  // RMSNorm row scales (row_scale mode)
+    const float *rs = p.f.row_ss ? s_rscale : nullptr;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // The next kernel may launch once every CTA of this grid has started.
@@ -497,6 +627,36 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
         __syncwarp();
     } else if (warp == CW + 1) {  // ----------------------------- group sums
         pdl_wait();
+        if (p.f.row_ss) {
+            // Row scales rsqrt(sum_k h^2 / K + eps) of the unnormalised
+            // activations from their per-16-column sums of squares: lane l
+            // adds tiles l, l + 32, ... for every row at once (one row of 32
+            // floats per tile, all loads in flight), then a butterfly per row
+            // -- the RMSNorm prologue's order.  Published to the consumers by
+            // the first xsfull arrival below.
+            float acc[MAX_XR];
+#pragma unroll
+            for (int m = 0; m < MAX_XR; ++m) acc[m] = 0.0f;
+            for (int tl = lane; tl < p.f.ss_tiles; tl += 32) {
+                const float4 *row = reinterpret_cast<const float4 *>(p.f.row_ss + tl * kSsWidth);
+#pragma unroll
+                for (int q = 0; q < MAX_XR / 4; ++q) {
+                    const float4 v = __ldcg(row + q);
+                    acc[4 * q] += v.x;
+                    acc[4 * q + 1] += v.y;
+                    acc[4 * q + 2] += v.z;
+                    acc[4 * q + 3] += v.w;
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < MAX_XR; ++m) {
+                float sum = acc[m];
+#pragma unroll
+                for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                if (lane == 0 && m < p.M) s_rscale[m] = rsqrtf(sum / static_cast<float>(p.K) + p.f.eps);
+            }
+            __syncwarp();
+        }
         // X_g = sum_{k in g} x[m][k] for every activation row, once per CTA and
         // stage, via m16n8k16 MMAs with an all-ones A operand (rows equal).
         const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 1.0 pairs
@@ -683,9 +843,10 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
                     accf[nt][mt][2] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][1]));
                     accf[nt][mt][3] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][1] >> 32));
                 }
-            segment_epilogue<MT, NT, CW>(p, accf, blk, warp, g, t, tid);
+            segment_epilogue<MT, NT, CW>(p, accf, blk, warp, g, t, tid, rs);
         }
-        combine_blocks<ROWS, CW>(p, lo, hi, warp, lane, tid, abort);
+        combine_blocks<ROWS, CW>(p, lo, hi, warp, lane, tid, abort, rs);
+        if (p.f.epi == EPI_RESID_AR) ar_finish<ROWS, CW>(p, lo, hi, warp, lane, tid, abort);
     }
 }
 

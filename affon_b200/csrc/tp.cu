@@ -45,6 +45,7 @@ struct NcclApi {
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char *(*GetErrorString)(ncclResult_t) = nullptr;
     ncclResult_t (*GetVersion)(int *) = nullptr;
 };
@@ -78,6 +79,7 @@ NcclApi &nccl() {
         sym(api.CommFinalize, "ncclCommFinalize");
         sym(api.CommDestroy, "ncclCommDestroy");
         sym(api.AllReduce, "ncclAllReduce");
+        sym(api.AllGather, "ncclAllGather");
         sym(api.GetErrorString, "ncclGetErrorString");
         sym(api.GetVersion, "ncclGetVersion");
         api.loaded = ok;
@@ -130,6 +132,14 @@ struct TpState {
     int rank = 0, world = 1;
     double timeout_s = 60.0;
     bool aborted = false;
+    // Exchange buffers of the fused row-parallel reduction: this rank's
+    // buffer and every rank's mapping of theirs (CUDA IPC), each holding two
+    // regions of [world][max_rows][max_cols] f32 plus arrival flags.
+    void *xbuf = nullptr;
+    void *peer[kTpMaxWorld] = {};
+    size_t region_bytes = 0, recv_bytes = 0;
+    int max_rows = 0;
+    int64_t max_cols = 0;
 };
 
 namespace {
@@ -189,6 +199,11 @@ struct DevScope {
 void tp_release(affon_b200_ctx *ctx) {
     if (!ctx || !ctx->tp) return;
     TpState *t = ctx->tp;
+    // Every rank stops touching the exchange buffers before it leaves: the
+    // caller synchronises (tp_synchronize) before tearing the group down.
+    for (int r = 0; r < t->world; ++r)
+        if (t->peer[r] && r != t->rank) cudaIpcCloseMemHandle(t->peer[r]);
+    if (t->xbuf) cudaFree(t->xbuf);
     if (t->comm && !t->aborted) {
         // Finalize flushes outstanding work; bounded like every other wait
         // (wait_comm aborts the communicator when it fails).
@@ -200,6 +215,25 @@ void tp_release(affon_b200_ctx *ctx) {
     }
     delete t;
     ctx->tp = nullptr;
+}
+
+bool tp_bind_exchange(affon_b200_ctx *ctx, int region, int64_t rows, int64_t cols, int64_t units, QmvFusion *f,
+                      const char **why) {
+    TpState *t = ctx ? ctx->tp : nullptr;
+    if (!t || t->aborted) { *why = "no live tensor-parallel group"; return false; }
+    if (!t->xbuf) { *why = "no exchange buffers (affon_b200_tp_exchange_reserve)"; return false; }
+    if (region < 0 || region > 1) { *why = "exchange region must be 0 or 1"; return false; }
+    if (rows > t->max_rows || cols > t->max_cols) { *why = "projection larger than the reserved exchange"; return false; }
+    if (units > kTpMaxUnits) { *why = "too many row units for the exchange flags"; return false; }
+    f->tp_world = t->world;
+    f->tp_rank = t->rank;
+    for (int r = 0; r < t->world; ++r) {
+        char *base = static_cast<char *>(t->peer[r]) + region * t->region_bytes;
+        f->tp_recv[r] = reinterpret_cast<float *>(base);
+        f->tp_flags_peer[r] = reinterpret_cast<unsigned *>(base + t->recv_bytes);
+    }
+    f->tp_flags_local = f->tp_flags_peer[t->rank];
+    return true;
 }
 
 }  // namespace afb
@@ -265,6 +299,62 @@ int affon_b200_tp_init(affon_b200_ctx *ctx, int rank, int world, const void *uni
         return afb::set_error(rc, msg.c_str());
     }
     ctx->tp = t;
+    return AFFON_B200_OK;
+}
+
+int affon_b200_tp_exchange_reserve(affon_b200_ctx *ctx, int max_rows, int64_t max_cols) {
+    afb::clear_error();
+    int rc = afb::need_group(ctx);
+    if (rc) return rc;
+    if (max_rows <= 0 || max_rows > afb::kMaxQmvRows || max_cols <= 0)
+        return afb::set_error(AFFON_B200_INVALID_ARG, "tp_exchange_reserve: 0 < rows <= 32, cols > 0");
+    afb::TpState *t = ctx->tp;
+    if (t->world > afb::kTpMaxWorld) return afb::set_error(AFFON_B200_UNSUPPORTED, "tp_exchange_reserve: world > 8");
+    if (t->xbuf) return afb::set_error(AFFON_B200_INVALID_ARG, "tp_exchange_reserve: already reserved");
+    afb::DevScope dev(ctx->device);
+    const size_t recv = (size_t(t->world) * max_rows * size_t(max_cols) * 4 + 255) / 256 * 256;
+    const size_t region = recv + size_t(afb::kTpMaxUnits) * 4;
+    cudaError_t e = cudaMalloc(&t->xbuf, 2 * region);
+    if (e != cudaSuccess) return afb::set_cuda_error(e, "tp exchange cudaMalloc");
+    if ((e = cudaMemset(t->xbuf, 0, 2 * region)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess)
+        return afb::set_cuda_error(e, "tp exchange clear");
+    // Share the buffer: every rank's IPC handle, gathered through NCCL.
+    cudaIpcMemHandle_t mine;
+    if ((e = cudaIpcGetMemHandle(&mine, t->xbuf)) != cudaSuccess) return afb::set_cuda_error(e, "cudaIpcGetMemHandle");
+    char *dsend = nullptr, *drecv = nullptr;
+    if ((e = cudaMalloc(&dsend, sizeof mine)) != cudaSuccess ||
+        (e = cudaMalloc(&drecv, sizeof mine * t->world)) != cudaSuccess)
+        return afb::set_cuda_error(e, "tp exchange handles");
+    cudaIpcMemHandle_t all[afb::kTpMaxWorld];
+    e = cudaMemcpy(dsend, &mine, sizeof mine, cudaMemcpyHostToDevice);
+    ncclResult_t r = e == cudaSuccess ? nccl().AllGather(dsend, drecv, sizeof mine, ncclUint8, t->comm, ctx->stream)
+                                      : ncclInvalidArgument;
+    if (r != ncclSuccess && r != ncclInProgress) {
+        cudaFree(dsend);
+        cudaFree(drecv);
+        return afb::fmt_error(AFFON_B200_CUDA_ERROR, "tp exchange all-gather: %s", nccl().GetErrorString(r));
+    }
+    rc = afb::wait_comm(t, t->timeout_s, "exchange all-gather");
+    if (rc == AFFON_B200_OK) {
+        rc = affon_b200_tp_synchronize(ctx, t->timeout_s);
+        if (rc == AFFON_B200_OK && (e = cudaMemcpy(all, drecv, sizeof mine * t->world, cudaMemcpyDeviceToHost)) != cudaSuccess)
+            rc = afb::set_cuda_error(e, "tp exchange handles read");
+    }
+    cudaFree(dsend);
+    cudaFree(drecv);
+    if (rc) return rc;
+    for (int p = 0; p < t->world; ++p) {
+        if (p == t->rank) {
+            t->peer[p] = t->xbuf;
+            continue;
+        }
+        if ((e = cudaIpcOpenMemHandle(&t->peer[p], all[p], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess)
+            return afb::set_cuda_error(e, "cudaIpcOpenMemHandle");
+    }
+    t->region_bytes = region;
+    t->recv_bytes = recv;
+    t->max_rows = max_rows;
+    t->max_cols = max_cols;
     return AFFON_B200_OK;
 }
 

@@ -4,9 +4,11 @@ Every projection is a 4-bit (or 8-bit) affine group-quantized linear
 (`quantized_matmul` layout: codes packed little-endian into u32 along K,
 group 64, bf16 scale and bias), run by the decode qmv with the decoder's
 residual adds, SiLU-gated product and final argmax fused into its epilogue.
-RMSNorm is one small kernel that also writes the normalized activations in
-the qmv's column order; attention and the SiLU epilogue write theirs in that
-order directly.
+RMSNorm is fused: the embedding and each residual epilogue write the next
+projection's activations as bf16(h * gamma) in the qmv's column order, and
+that qmv multiplies each output row by rsqrt(mean(h^2) + eps), computed from
+the per-16-column sums of squares the same epilogue leaves; attention and the
+SiLU epilogue write their outputs in that order directly.
 Attention is the affon_b200 decode-attention kernel (RoPE and KV-cache
 append fused).  The reference has no quantized decoder; the layer structure
 follows its Llama program (packages/@affon/models/src/llama/model.ts:64-78:
@@ -22,11 +24,15 @@ epilogue sees both halves of each SiLU product in one thread.
 Tensor parallelism (`tp=(rank, world, group_id)`, one process per GPU): the
 full model is generated identically on every rank and each rank keeps its
 shard (affon_b200.tp describes the split).  QKV, gate/up and the LM head are
-column-parallel; O and down are row-parallel: they write f32 partial sums,
-an NCCL sum all-reduce combines them, and one kernel adds the sum to the
-residual stream and normalises it for the next projection.  The LM head's
-local argmax keys carry global vocabulary indices and a max all-reduce picks
-the winner, so every rank samples the same tokens.
+column-parallel; O and down are row-parallel.  By default (`tp_reduce="p2p"`)
+each row-parallel qmv is fused with its all-reduce: it pushes its f32 rows
+into every rank's exchange buffer over NVLink, waits (bounded) for the other
+ranks' rows, sums them in rank order and applies the residual epilogue, so a
+step has the same five launches per layer as on one GPU.  `tp_reduce="nccl"`
+runs an NCCL sum all-reduce of the partial outputs and a residual-add +
+RMSNorm kernel instead.  The LM head's local argmax keys carry global
+vocabulary indices and an NCCL max all-reduce picks the winner, so every rank
+samples the same tokens.
 
 A decode step is captured once in a CUDA graph: the current position,
 step counter and tokens live in device memory and are advanced by the last
@@ -157,7 +163,7 @@ class QuantizedDecoder:
     affon_b200.tp.unique_id on rank 0, shared with every rank)."""
 
     def __init__(self, cfg, batch, capacity, device, seed=0, max_steps=4096, workspace_bytes=None, overlap=False,
-                 tp=None):
+                 tp=None, tp_reduce="p2p"):
         if batch > _lib.MAX_QMV_ROWS:
             raise ValueError(f"decode qmv handles up to {_lib.MAX_QMV_ROWS} rows per step")
         self.cfg, self.B, self.cap = cfg, batch, capacity
@@ -220,8 +226,13 @@ class QuantizedDecoder:
         self._overlap = overlap
         check(L.affon_b200_ctx_set_overlap(self.ctx, 1 if overlap else 0))
         self.tp = None
+        if tp_reduce not in ("p2p", "nccl"):
+            raise ValueError("tp_reduce must be 'p2p' or 'nccl'")
+        self.tp_reduce = tp_reduce if world > 1 else None
         if world > 1:
             self.tp = tpmod.TensorParallel(self.ctx, rank, world, tp[2], *(tp[3:4] or [60.0]))
+            if tp_reduce == "p2p":
+                check(L.affon_b200_tp_exchange_reserve(self.ctx, batch, c.d_model), "tp_exchange_reserve")
         self._build_calls()
         self.graph = None
         self._pos_host = 0   # host copy of the device position, to refuse steps beyond capacity
@@ -238,39 +249,52 @@ class QuantizedDecoder:
         pair = 1 if c.bits == 4 else 0          # producers write the 4-bit qmv's pair order
         self.attn_desc.out_pair_order = pair
         fz = lambda **kw: _lib.QmvFusion(struct_size=ctypes.sizeof(_lib.QmvFusion), x_mode=1, **kw)
-        silu = fz(epilogue=_lib.EPI_SILU_MUL, act=ptr(self.act), ld_act=self.act.shape[1], act_pair_order=pair)
+        # RMSNorm fused into the consumer: x = bf16(h * gamma) written by the
+        # embedding or the previous residual epilogue, and the consumer qmv
+        # scales each output row by rsqrt(mean(h^2) + eps) from the sums of
+        # squares (row-scale mode).
+        scaled = dict(row_ss=ptr(self.ss), ss_tiles=c.d_model // 16, eps=c.eps)
+        silu = dict(epilogue=_lib.EPI_SILU_MUL, act=ptr(self.act), ld_act=self.act.shape[1], act_pair_order=pair)
         xq = ptr(self.xq)
         self.calls = []
         tp = self.world > 1
-        resid = dict(epilogue=_lib.EPI_RESID, h_out=ptr(self.h), ld_h_out=c.d_model, ss_out=ptr(self.ss))
+        nccl = self.tp_reduce == "nccl"
+        resid = lambda gamma, region=None: dict(
+            epilogue=_lib.EPI_RESID if region is None else _lib.EPI_RESID_AR, h_out=ptr(self.h), ld_h_out=c.d_model,
+            ss_out=ptr(self.ss), next_gamma=ptr(gamma), next_x=xq, ld_next_x=c.d_model, next_pair_order=pair,
+            exchange_region=region or 0)
+        self.embed_gamma = self.layers[0]["attn_norm"]
         for i, lay in enumerate(self.layers):
             q, o, gu, dn = lay["qkv"], lay["o"], lay["gate_up"], lay["down"]
             nxt = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.final_norm
-            if not tp or i == 0:
-                self.calls.append(("norm", lay["attn_norm"]))
-            self.calls.append(("qmv", q.desc(B), xq, q, ptr(self.qkv), fz(epilogue=_lib.EPI_STORE)))
+            # QKV and gate/up read bf16(h * gamma) and apply the row scale,
+            # except after an NCCL all-reduce (resid_norm writes normalised x)
+            qkv_scaled = (not nccl) or i == 0
+            self.calls.append(("qmv", q.desc(B), xq, q, ptr(self.qkv),
+                               fz(epilogue=_lib.EPI_STORE, **(scaled if qkv_scaled else {}))))
             self.calls.append(("attn", i))
-            if tp:
+            if nccl:
                 self.calls.append(("qmv", o.desc(B, y_dtype=_lib.F32), ptr(self.attn), o, ptr(self.y),
                                    fz(epilogue=_lib.EPI_STORE)))
                 self.calls.append(("allreduce", self.y, "sum"))
                 self.calls.append(("resid_norm", lay["ffn_norm"]))
-            else:
-                self.calls.append(("qmv", o.desc(B), ptr(self.attn), o, None, fz(**resid)))
-                self.calls.append(("norm", lay["ffn_norm"]))
-            self.calls.append(("qmv", gu.desc(B), xq, gu, None, silu))
-            if tp:
+                self.calls.append(("qmv", gu.desc(B), xq, gu, None, fz(**silu)))
                 self.calls.append(("qmv", dn.desc(B, y_dtype=_lib.F32), ptr(self.act), dn, ptr(self.y),
                                    fz(epilogue=_lib.EPI_STORE)))
                 self.calls.append(("allreduce", self.y, "sum"))
                 self.calls.append(("resid_norm", nxt))
             else:
-                self.calls.append(("qmv", dn.desc(B), ptr(self.act), dn, None, fz(**resid)))
+                # row-parallel O and down fused with their all-reduce under
+                # tensor parallelism (exchange regions alternate)
+                self.calls.append(("qmv", o.desc(B), ptr(self.attn), o, None,
+                                   fz(**resid(lay["ffn_norm"], 0 if tp else None))))
+                self.calls.append(("qmv", gu.desc(B), xq, gu, None, fz(**silu, **scaled)))
+                self.calls.append(("qmv", dn.desc(B), ptr(self.act), dn, None,
+                                   fz(**resid(nxt, 1 if tp else None))))
         lm = self.lm_head
-        if not tp:
-            self.calls.append(("norm", self.final_norm))
         self.calls.append(("qmv", lm.desc(B), xq, lm, None,
-                           fz(epilogue=_lib.EPI_ARGMAX, amax=ptr(self.amax), index_offset=self.vocab_offset)))
+                           fz(epilogue=_lib.EPI_ARGMAX, amax=ptr(self.amax), index_offset=self.vocab_offset,
+                              **({} if nccl else scaled))))
         if tp:
             self.calls.append(("allreduce", self.amax, "max"))
         self._kv_layer = [(self.k_cache[i], self.v_cache[i]) for i in range(c.layers)]
@@ -286,7 +310,9 @@ class QuantizedDecoder:
         stream = torch.cuda.current_stream(self.device) if events else None
         mark = (lambda i: events[i].record(stream)) if events else (lambda i: None)
         check(L.affon_b200_embed(ctx, self.embed.data_ptr(), c.d_model, c.vocab, self.tokens.data_ptr(), self.B,
-                                 c.d_model, self.h.data_ptr(), self.ss.data_ptr(), self.amax.data_ptr()), "embed")
+                                 c.d_model, self.h.data_ptr(), self.ss.data_ptr(), self.amax.data_ptr(),
+                                 self.embed_gamma.data_ptr(), self.xq.data_ptr(), c.d_model,
+                                 1 if c.bits == 4 else 0), "embed")
         mark(1)
         for ci, call in enumerate(self.calls):
             kind = call[0]
@@ -427,7 +453,9 @@ class QuantizedDecoder:
         if role == "embed":
             return lambda: check(L.affon_b200_embed(ctx, self.embed.data_ptr(), c.d_model, c.vocab,
                                                     self.tokens.data_ptr(), self.B, c.d_model, self.h.data_ptr(),
-                                                    self.ss.data_ptr(), self.amax.data_ptr()))
+                                                    self.ss.data_ptr(), self.amax.data_ptr(),
+                                                    self.embed_gamma.data_ptr(), self.xq.data_ptr(), c.d_model,
+                                                    1 if c.bits == 4 else 0))
         if role == "finalize":
             def fin():
                 check(L.affon_b200_argmax_finalize(ctx, self.amax.data_ptr(), self.B, self.tokens.data_ptr(), None, 0,

@@ -246,6 +246,29 @@ typedef struct affon_b200_qmv_fusion {
     int64_t ld_act;
     unsigned long long *amax;
     int64_t index_offset; /* epilogue 3: added to n in the key (the first row of a vocabulary shard) */
+    /* Row-scale mode (row_ss != NULL): x holds bf16(h * gamma), the
+     * activations before RMSNorm's row scale, and every output of row m is
+     * multiplied by rsqrt(sum_k h[m][k]^2 / K + eps) -- the fused RMSNorm --
+     * with the sums of squares from row_ss ([ss_tiles][32] partial sums). */
+    const float *row_ss;
+    int32_t ss_tiles;
+    float eps;
+    /* Epilogue 1 extra output (next_x != NULL): next_x[m][c(n)] =
+     * bf16(h_out[m][n] * next_gamma[n]) after the residual update, c(n) in
+     * the 4-bit pair order when next_pair_order -- the next projection's
+     * row-scale-mode activations. */
+    const void *next_gamma;
+    void *next_x;
+    int64_t ld_next_x;
+    int32_t next_pair_order;
+    /* Epilogue 4 (tensor parallel, after affon_b200_tp_exchange_reserve):
+     * epilogue 1 applied to the sum over the group of every rank's y -- a
+     * row-parallel projection fused with its all-reduce.  Each rank pushes its
+     * rows into every rank's exchange buffer (NVLink stores), counts them on
+     * per-row-unit flags, waits (bounded) for all ranks' pushes of the rows it
+     * finalises and sums them in rank order, so every rank holds the same h.
+     * Consecutive fused calls must alternate exchange_region 0 and 1. */
+    int32_t exchange_region;
 } affon_b200_qmv_fusion;
 
 int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, const void *x, const uint32_t *w,
@@ -281,9 +304,12 @@ int affon_b200_decode_attention(affon_b200_ctx *ctx, const affon_b200_attn_desc 
 /* h[b][:] = f32(table[tokens[b]][:]) with ss_out[dim/16][32] partial sums of
  * squares for the first norm; also zeroes amax[0..batch).  batch <= 32.  A
  * token outside [0, vocab) reads row 0 and makes the next
- * affon_b200_ctx_synchronize return AFFON_B200_INVALID_ARG. */
+ * affon_b200_ctx_synchronize return AFFON_B200_INVALID_ARG.  When gamma is
+ * given, also x[b][c(k)] = bf16(h[b][k] * gamma[k]) (the first projection's
+ * row-scale-mode activations; c in the 4-bit pair order when pair_order). */
 int affon_b200_embed(affon_b200_ctx *ctx, const void *table, int64_t ld_table, int64_t vocab, const int *tokens,
-                     int batch, int dim, float *h, float *ss_out, unsigned long long *amax);
+                     int batch, int dim, float *h, float *ss_out, unsigned long long *amax, const void *gamma,
+                     void *x, int64_t ld_x, int pair_order);
 
 /* tokens[b] = argmax index held in amax[b]; history[*step % history_rows][b]
  * = tokens[b] (history may be NULL; it keeps the last history_rows steps);
@@ -320,6 +346,11 @@ int affon_b200_tp_id_check(const void *id);
 int affon_b200_tp_init(affon_b200_ctx *ctx, int rank, int world, const void *id, double timeout_s);
 int affon_b200_tp_rank(const affon_b200_ctx *ctx);   /* -1 without a group */
 int affon_b200_tp_world(const affon_b200_ctx *ctx);  /* 0 without a group */
+/* Exchange buffers for the fused row-parallel qmv (epilogue 4): two regions
+ * of [world][max_rows][max_cols] f32 per rank, mapped by every rank through
+ * CUDA IPC (handles gathered over the group).  Collective: every rank calls
+ * it with the same sizes. */
+int affon_b200_tp_exchange_reserve(affon_b200_ctx *ctx, int max_rows, int64_t max_cols);
 /* In-place all-reduce of `count` elements on the context's stream: f32 or
  * bf16 sum, or u64 max. */
 int affon_b200_tp_allreduce(affon_b200_ctx *ctx, void *buf, size_t count, int dtype, int op);

@@ -32,6 +32,14 @@ def rope(x, cos, sin):  # x [..., 128]; rotate-half pairs (d, d+64)
     return torch.cat([a * cos - b * sin, b * cos + a * sin], dim=-1)
 
 
+def normed_proj(h, g, lin, eps):
+    """RMSNorm fused into a projection as the decoder computes it: the
+    projection reads bf16(h * gamma) and its output rows are scaled by
+    rsqrt(mean(h^2) + eps)."""
+    r = torch.rsqrt((h * h).mean(dim=-1, keepdim=True) + eps)
+    return r * (bf16(h * g.float()) @ lin.dequantized().T)
+
+
 def ref_step(dec, tokens, pos, kc, vc):
     """One decode step in float32 (bf16 roundings where the kernels store bf16).
     kc/vc: float32 copies of the caches [L][B][kvh][cap][hd], updated in place."""
@@ -40,8 +48,7 @@ def ref_step(dec, tokens, pos, kc, vc):
     h = dec.embed[tokens.long()].float()
     cos, sin = dec.cos[pos], dec.sin[pos]
     for li, lay in enumerate(dec.layers):
-        xn = rms_norm(h, lay["attn_norm"], c.eps)
-        qkv = bf16(xn @ lay["qkv"].dequantized().T)
+        qkv = bf16(normed_proj(h, lay["attn_norm"], lay["qkv"], c.eps))
         q = qkv[:, :c.q_heads * hd].reshape(B, c.q_heads, hd)
         k = qkv[:, c.q_heads * hd:(c.q_heads + c.kv_heads) * hd].reshape(B, c.kv_heads, hd)
         v = qkv[:, (c.q_heads + c.kv_heads) * hd:].reshape(B, c.kv_heads, hd)
@@ -56,14 +63,12 @@ def ref_step(dec, tokens, pos, kc, vc):
         p = torch.softmax(scores, dim=-1)
         attn = bf16(torch.einsum("bht,bhtd->bhd", p, vq).reshape(B, -1))
         h = h + attn @ lay["o"].dequantized().T
-        xn2 = rms_norm(h, lay["ffn_norm"], c.eps)
-        gu = xn2 @ lay["gate_up"].dequantized().T                       # interleaved tiles of 8 gate + 8 up rows
+        gu = normed_proj(h, lay["ffn_norm"], lay["gate_up"], c.eps)     # interleaved tiles of 8 gate + 8 up rows
         gu = gu.reshape(B, -1, 2, 8)
         gate, up = gu[:, :, 0, :].reshape(B, -1), gu[:, :, 1, :].reshape(B, -1)
         act = bf16(torch.nn.functional.silu(gate) * up)
         h = h + act @ lay["down"].dequantized().T
-    xf = rms_norm(h, dec.final_norm, c.eps)
-    logits = xf @ dec.lm_head.dequantized().T
+    logits = normed_proj(h, dec.final_norm, dec.lm_head, c.eps)
     return h, logits
 
 

@@ -86,14 +86,14 @@ def _finish(store, rank):
             time.sleep(0.01)
 
 
-def _tp_vs_single(rank, port):
+def _tp_vs_single(rank, port, reduce):
     from affon_b200.decoder import LlamaConfig, QuantizedDecoder
     cfg = LlamaConfig(**SMALL_TP)
     store, uid = _group(rank, port)
     dev = torch.device("cuda", rank)
     gen = torch.Generator().manual_seed(3)
     prompt = torch.randint(0, cfg.vocab, (12, 4), generator=gen)
-    dec = QuantizedDecoder(cfg, 4, 64, dev, seed=1, max_steps=16, tp=(rank, 2, uid, 60.0))
+    dec = QuantizedDecoder(cfg, 4, 64, dev, seed=1, max_steps=16, tp=(rank, 2, uid, 60.0), tp_reduce=reduce)
     try:
         dec.prefill(prompt)                         # eager steps, positions 0..11
         dec.synchronize(30.0)
@@ -169,9 +169,79 @@ def _peer_leaves(rank, port):
             _finish(store, rank)
 
 
+def _fused_allreduce(rank, port):
+    """One row-parallel qmv fused with its all-reduce (epilogue 4) on a K
+    shard per rank, against the unsharded product on one GPU."""
+    import ctypes
+    import numpy as np
+    from affon_b200 import _lib, synthetic
+    from affon_b200 import tp as tpmod
+    from affon_b200.core import check
+    store, uid = _group(rank, port)
+    dev = torch.device("cuda", rank)
+    L = _lib.lib()
+    ctx = ctypes.c_void_p()
+    check(L.affon_b200_ctx_create(rank, None, ctypes.byref(ctx)))
+    tpg = tpmod.TensorParallel(ctx, rank, 2, uid, 30.0)
+    res = {}
+    try:
+        check(L.affon_b200_ctx_set_stream(ctx, torch.cuda.current_stream(dev).cuda_stream))
+        M, N, K = 16, 4096, 4096
+        check(L.affon_b200_tp_exchange_reserve(ctx, M, N))
+        d = synthetic.quantized_linear(M, N, K, bits=4, seed=77)
+        k0, k1 = tpmod.k_split(K, rank, 2, 4)
+        w, sc, b = tpmod.slice_linear_k(d["w"], d["s"], d["b"], k0, k1, 4)
+        up = lambda a, t: torch.from_numpy(np.ascontiguousarray(a).view(t)).to(dev)
+        x = up(d["x"][:, k0:k1], np.int16)
+        wt, st, bt = up(w, np.int32), up(sc, np.int16), up(b, np.int16)
+        h = torch.linspace(-1, 1, M * N, device=dev).reshape(M, N).contiguous()
+        h0 = h.clone()
+        ss = torch.zeros((N // 16, 32), device=dev)
+        desc = _lib.QmmDesc()
+        desc.struct_size = ctypes.sizeof(_lib.QmmDesc)
+        desc.bits, desc.group_size = 4, 64
+        desc.x_dtype = desc.param_dtype = desc.y_dtype = _lib.BF16
+        Kl = k1 - k0
+        desc.x = _lib.View(M, Kl, Kl, 1, 0)
+        desc.w = _lib.View(N, Kl // 8, Kl // 8, 1, 0)
+        desc.s = desc.b = _lib.View(N, Kl // 64, Kl // 64, 1, 0)
+        desc.y = _lib.View(M, N, N, 1, 0)
+        for region in (0, 1, 0):                      # three calls: regions alternate, flags reset
+            fz = _lib.QmvFusion(struct_size=ctypes.sizeof(_lib.QmvFusion), x_mode=0, epilogue=_lib.EPI_RESID_AR,
+                                h_out=h.data_ptr(), ld_h_out=N, ss_out=ss.data_ptr(), exchange_region=region)
+            check(L.affon_b200_qmv_fused(ctx, ctypes.byref(desc), x.data_ptr(), wt.data_ptr(), st.data_ptr(),
+                                         bt.data_ptr(), None, ctypes.byref(fz)))
+        tpg.synchronize(30.0)
+        res["h"] = h.cpu()
+        res["h0"] = h0.cpu()
+        res["ss"] = ss.cpu()
+    finally:
+        tpg.destroy()
+        L.affon_b200_ctx_destroy(ctx)
+    if rank == 0:
+        import oracle
+        d = synthetic.quantized_linear(16, 4096, 4096, bits=4, seed=77)
+        res["ref"] = torch.from_numpy(oracle.qmm_dense(d["x"], "bf16", d["w"], d["s"], d["b"], "bf16", 16, 4096,
+                                                       4096, 4, 64, threads=oracle.cpu_threads()))
+    _finish(store, rank)
+    return res
+
+
 @needs2
-def test_tp2_decoder_matches_single_gpu():
-    out = _spawn(_tp_vs_single)
+def test_tp2_fused_row_parallel_allreduce():
+    out = _spawn(_fused_allreduce)
+    for r in (0, 1):
+        assert not (isinstance(out.get(r), tuple) and out[r][0] == "error"), out.get(r)
+    r0, r1 = out[0], out[1]
+    assert torch.equal(r0["h"], r1["h"]) and torch.equal(r0["ss"], r1["ss"])   # replicated, bit for bit
+    want = r0["h0"] + 3 * r0["ref"]
+    assert float((r0["h"] - want).abs().max()) <= 1e-4 * max(1.0, float(want.abs().max()))
+
+
+@needs2
+@pytest.mark.parametrize("reduce", ["p2p", "nccl"])
+def test_tp2_decoder_matches_single_gpu(reduce):
+    out = _spawn(_tp_vs_single, reduce)
     for r in (0, 1):
         assert not (isinstance(out.get(r), tuple) and out[r][0] == "error"), out.get(r)
     r0, r1 = out[0], out[1]
