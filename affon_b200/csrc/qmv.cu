@@ -204,13 +204,16 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *a) {
 
 // EPI_RESID_AR: after the consumer warps pushed the rows of one unit (a
 // whole block, or this CTA's share of a shared block), count the unit's
-// arrival on every rank.  Called by all consumer threads.
+// arrival on every rank: the CTA barrier orders every thread's pushes before
+// thread 0's system-scope fence (cumulative), which orders them before its
+// increments of the peers' flags.  Called by all consumer threads.
 template <int CW>
 __device__ __forceinline__ void ar_signal(const Params &p, int unit, int tid) {
-    __threadfence_system();
     named_bar_sync(1, CW * 32);
     if (tid == 0) {
-        for (int r = 0; r < p.f.tp_world; ++r) atomicAdd_system(p.f.tp_flags_peer[r] + unit, 1u);
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int r = 0; r < p.f.tp_world; ++r)
+            asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(p.f.tp_flags_peer[r] + unit) : "memory");
     }
 }
 
@@ -486,23 +489,22 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
     }
 }
 
-// EPI_RESID_AR, last phase: for every unit this CTA pushed, wait (bounded)
-// until every rank has pushed the same rows, then sum them in rank order and
-// apply the residual update.  Every rank finalises the same units with the
-// same plan, so a unit's flag reaches the world size exactly once per launch;
-// the waiter resets it.
+// EPI_RESID_AR, last phase: wait (bounded) until every rank has pushed the
+// rows of every unit this CTA finalised, then sum them in rank order and apply
+// the residual update.  Every rank finalises the same units with the same
+// plan, so a unit's flag reaches the world size exactly once per launch; the
+// waiter resets it (no rank touches it again in this launch).
 template <int ROWS, int CW>
 __device__ void ar_finish(const Params &p, int64_t lo, int64_t hi, int warp, int lane, int tid, volatile int *abort) {
     constexpr int CT = CW * 32, TILES = ROWS / 16;
     if (hi <= lo) return;
     const int b_first = static_cast<int>(lo / p.spb), b_last = static_cast<int>((hi - 1) / p.spb);
-    for (int blk = b_first; blk <= b_last; ++blk) {
-        int first, total;
-        block_contributors(p, blk, first, total);
-        const int slot = total == 1 ? 0 : static_cast<int>(blockIdx.x) - first;
-        const int unit = blk * p.max_slots + slot;
-        if (tid == 0) {
-            const uint64_t start = globaltimer();
+    if (tid == 0) {
+        const uint64_t start = globaltimer();
+        for (int blk = b_first; blk <= b_last; ++blk) {
+            int first, total;
+            block_contributors(p, blk, first, total);
+            const int unit = blk * p.max_slots + (total == 1 ? 0 : static_cast<int>(blockIdx.x) - first);
             while (ld_acquire_sys(p.f.tp_flags_local + unit) < static_cast<unsigned>(p.f.tp_world)) {
                 if (*abort || globaltimer() - start > p.arrival_wait_ns) {
                     *abort = 1;
@@ -511,15 +513,20 @@ __device__ void ar_finish(const Params &p, int64_t lo, int64_t hi, int warp, int
                 }
                 __nanosleep(64);
             }
-            p.f.tp_flags_local[unit] = 0u;  // no rank touches it again in this launch
+            p.f.tp_flags_local[unit] = 0u;
         }
-        named_bar_sync(1, CT);
         asm volatile("fence.acq_rel.sys;" ::: "memory");
+    }
+    named_bar_sync(1, CT);
+    const int64_t src_stride = static_cast<int64_t>(p.M) * p.N;
+    const float *recv = p.f.tp_recv[p.f.tp_rank];
+    for (int blk = b_first; blk <= b_last; ++blk) {
+        int first, total;
+        block_contributors(p, blk, first, total);
+        const int slot = total == 1 ? 0 : static_cast<int>(blockIdx.x) - first;
         const int t0 = total == 1 ? 0 : slot * TILES / total, t1 = total == 1 ? TILES : (slot + 1) * TILES / total;
         const int row0 = t0 * 16, nrows = (t1 - t0) * 16;
         const int units = ((nrows + 31) / 32) * p.M;
-        const int64_t src_stride = static_cast<int64_t>(p.M) * p.N;
-        const float *recv = p.f.tp_recv[p.f.tp_rank];
         for (int u = warp; u < units; u += CW) {
             const int chunk = u / p.M, m = u - chunk * p.M;
             const int rr = chunk * 32 + lane;
