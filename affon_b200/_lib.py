@@ -77,6 +77,7 @@ SIGNATURES = {
     "affon_b200_qmv_noalloc_status": ([c_vp, ctypes.POINTER(c_u32)], c_i32),
     "affon_b200_ctx_set_overlap": ([c_vp, c_i32], c_i32),
     "affon_b200_debug_set_combine_wait": ([ctypes.c_uint64, c_u32], c_i32),
+    "affon_b200_debug_set_slice_rows": ([ctypes.c_int64], c_i32),
     "affon_b200_qmv_fused": ([c_vp, ctypes.POINTER(QmmDesc), c_vp, c_vp, c_vp, c_vp, c_vp,
                               ctypes.POINTER(QmvFusion)], c_i32),
     "affon_b200_qmv_prep": ([c_vp, c_i32, c_vp, c_i64, c_vp, c_i32, c_vp, ctypes.c_float, c_i32, c_i32, c_i32, c_vp,

@@ -142,7 +142,7 @@ afb::QmmArgs make_args(const affon_b200_qmm_desc *d, const void *x, const void *
     return a;
 }
 
-enum Impl { IMPL_GENERIC = 0, IMPL_QMV = 1, IMPL_QMM_TC = 2 };
+enum Impl { IMPL_GENERIC = 0, IMPL_QMV = 1, IMPL_QMM_TC = 2, IMPL_QMM_EXACT = 3 };
 
 struct Choice {
     Impl impl;
@@ -165,6 +165,12 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
     const bool qmv_ok = afb::qmv_supported(probe, &why_qmv);
     const char *why_tc = "";
     const bool tc_ok = afb::qmm_tc_supported(a, &why_tc);
+    const char *why_exact = "";
+    bool exact_ok = afb::qmm_exact_supported(a, &why_exact);
+    if (exact_ok && afb::qmm_exact_min_workspace(a) > workspace) {
+        exact_ok = false;
+        why_exact = "qmm_exact: the context workspace is too small";
+    }
     afb::QmvPlan qplan{};
     if (qmv_ok) qplan = afb::qmv_plan(probe, num_sms, workspace);
     const bool qmv_plannable = qmv_ok && qplan.splits > 0;
@@ -175,17 +181,21 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
         snprintf(reason, sizeof reason,
                  "M=%lld <= 32: decode qmv, stream-K over %d CTAs, up to %d K segments per tile, %d-stage ring",
                  (long long)a.M, c.plan.grid_n, c.plan.max_slots, c.plan.stages);
-    } else if (tc_ok && (d->numerical_policy == AFFON_B200_POLICY_APPROXIMATE || a.y_bf16)) {
+    } else if (tc_ok && d->numerical_policy == AFFON_B200_POLICY_APPROXIMATE) {
         c.impl = IMPL_QMM_TC;
         snprintf(reason, sizeof reason, "M=%lld >= 64: tcgen05 qmm with bf16-rounded decoded weights", (long long)a.M);
+    } else if (exact_ok) {
+        c.impl = IMPL_QMM_EXACT;
+        snprintf(reason, sizeof reason,
+                 "M=%lld >= 64: tcgen05 qmm on exact codes, per-group f32 scales, bias term on tensor cores",
+                 (long long)a.M);
     } else if (qmv_plannable && (a.M <= 64 || d->numerical_policy != AFFON_B200_POLICY_APPROXIMATE)) {
         c.impl = IMPL_QMV;
         c.passes = static_cast<int>((a.M + afb::kMaxQmvRows - 1) / afb::kMaxQmvRows);
         c.plan = qplan;
         snprintf(reason, sizeof reason, "M=%lld > 32: %d qmv passes over 32-row slices", (long long)a.M, c.passes);
     } else {
-        snprintf(reason, sizeof reason, "generic strided kernel (%s%s%s)", why_qmv, tc_ok ? "" : "; ",
-                 tc_ok ? "" : why_tc);
+        snprintf(reason, sizeof reason, "generic strided kernel (%s; %s)", why_qmv, why_exact);
     }
     if (sel) {
         memset(sel, 0, sizeof *sel);
@@ -195,6 +205,9 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
         else if (c.impl == IMPL_QMM_TC)
             snprintf(sel->implementation_id, sizeof sel->implementation_id,
                      "cuda_quantized_matmul.sm100_qmm_tcgen05_b%d_g64", d->bits);
+        else if (c.impl == IMPL_QMM_EXACT)
+            snprintf(sel->implementation_id, sizeof sel->implementation_id,
+                     "cuda_quantized_matmul.sm100_qmm_tcgen05_exact_b%d_g64", d->bits);
         else
             snprintf(sel->implementation_id, sizeof sel->implementation_id, "cuda_quantized_matmul.sm100_generic");
         sel->implementation_version = 1;
@@ -227,6 +240,9 @@ int launch(affon_b200_ctx *ctx, const afb::QmmArgs &a, const Choice &c) {
     }
     case IMPL_QMM_TC:
         e = afb::launch_qmm_tc(a, ctx->workspace, ctx->stream);
+        break;
+    case IMPL_QMM_EXACT:
+        e = afb::launch_qmm_exact(a, ctx->workspace, ctx->workspace_bytes, ctx->stream);
         break;
     default:
         e = afb::launch_qmm_generic(a, ctx->stream);
@@ -330,6 +346,12 @@ int affon_b200_ctx_set_overlap(affon_b200_ctx *ctx, int enable) {
 
 int affon_b200_debug_set_combine_wait(uint64_t limit_ns, uint32_t extra_arrivals) {
     afb::qmv_set_combine_wait(limit_ns, extra_arrivals);
+    return AFFON_B200_OK;
+}
+
+int affon_b200_debug_set_slice_rows(int64_t rows) {
+    if (rows < 0) return fail(AFFON_B200_INVALID_ARG, "slice rows must be >= 0");
+    afb::qmm_exact_set_slice_cap(rows);
     return AFFON_B200_OK;
 }
 

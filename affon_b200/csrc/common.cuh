@@ -51,6 +51,27 @@ AFB_DEVICE uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return d;
 }
 
+// Natural-order exact bf16 code pairs of a 4-bit word: (q0,q1), (q2,q3),
+// (q4,q5), (q6,q7).  Even nibbles are gathered into the low half-word and odd
+// ones into the high half-word (two delta swaps); each pair is then the bf16
+// pair (128+q, 128+q') built by one logic op, minus 128 (exact).
+AFB_DEVICE void dec4_nat(uint32_t w, uint32_t (&out)[4]) {
+    uint32_t t = (w ^ (w >> 4)) & 0x00F000F0u;
+    w ^= t ^ (t << 4);
+    t = (w ^ (w >> 8)) & 0x0000FF00u;
+    w ^= t ^ (t << 8);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        out[i] = bf16x2_sub(lop3_and_or(w >> (4 * i), 0x000F000Fu, 0x43004300u), 0x43004300u);
+}
+// Bytes i and i+1 of an 8-bit word as an exact bf16 pair (q, q'), through
+// the f32 2^23 + q trick.
+AFB_DEVICE uint32_t dec8_pair(uint32_t w, int i) {
+    float f0 = __uint_as_float(prmt(w, 0x4B000000u, 0x7540u + i)) - 8388608.0f;
+    float f1 = __uint_as_float(prmt(w, 0x4B000000u, 0x7540u + i + 1)) - 8388608.0f;
+    return pack_bf16x2(f0, f1);
+}
+
 // Streaming loads of packed weights: read-only path, no L1 allocation.
 AFB_DEVICE uint2 ldg_stream_v2(const void *p) {
     uint2 v;

@@ -153,6 +153,16 @@ cudaError_t launch_finalize(const unsigned long long *amax, int B, int *tokens, 
 bool qmm_tc_supported(const QmmArgs &a, const char **why);
 cudaError_t launch_qmm_tc(const QmmArgs &a, void *workspace, cudaStream_t stream);
 
+// Prefill qmm with reassociated numerics on tcgen05 tensor cores (M >= 64,
+// bf16 x/s/b, 4/8-bit, group 64): exact codes, per-group f32 scales, the bias
+// term as a tensor-core product with exact bf16 pieces of the group sums.
+// Needs at least qmm_exact_min_workspace(a) bytes of workspace; larger M is
+// processed in row slices that fit.
+bool qmm_exact_supported(const QmmArgs &a, const char **why);
+size_t qmm_exact_min_workspace(const QmmArgs &a);
+cudaError_t launch_qmm_exact(const QmmArgs &a, void *workspace, size_t workspace_bytes, cudaStream_t stream);
+void qmm_exact_set_slice_cap(int64_t rows);  // test hook: most rows per pass (0 = workspace bound)
+
 void count_launch(uint64_t n = 1);
 
 }  // namespace afb

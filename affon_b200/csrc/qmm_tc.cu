@@ -66,23 +66,6 @@ struct Cfg {
     static constexpr int SMEM = 1024 + STAGES * (X_BYTES + A_BYTES) + PSTAGES * P_BYTES + 512;
 };
 
-// Natural-order bf16 pairs of a 4-bit word: (q0,q1), (q2,q3), (q4,q5), (q6,q7).
-// Even nibbles are gathered into the low half-word and odd ones into the high
-// half-word (two delta swaps), then the 128+q bf16 trick extracts each pair.
-__device__ __forceinline__ void dec4_nat(uint32_t w, uint32_t (&out)[4]) {
-    uint32_t t = (w ^ (w >> 4)) & 0x00F000F0u;
-    w ^= t ^ (t << 4);
-    t = (w ^ (w >> 8)) & 0x0000FF00u;
-    w ^= t ^ (t << 8);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        out[i] = bf16x2_sub(lop3_and_or(w >> (4 * i), 0x000F000Fu, 0x43004300u), 0x43004300u);
-}
-__device__ __forceinline__ uint32_t dec8_pair(uint32_t w, int i) {
-    float f0 = __uint_as_float(prmt(w, 0x4B000000u, 0x7540u + i)) - 8388608.0f;
-    float f1 = __uint_as_float(prmt(w, 0x4B000000u, 0x7540u + i + 1)) - 8388608.0f;
-    return pack_bf16x2(f0, f1);
-}
 __device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;
     asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -270,7 +253,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int c = 0; c < ACC_COLS / 16; ++c) {
                 uint32_t r[16];
                 tmem_ld_32x32b_x16(base + c * 16, r);
-                tmem_wait_ld();
+                tmem_wait_ld(r);
                 const int m0 = mb * BX + c * 16;
                 if (n < p.N) {
 #pragma unroll

@@ -278,9 +278,11 @@ def ncu_traffic(key):
 
 def kernel_keys(dev, pk):
     """Stand-alone kernel figures measured in the same run: the LM-head qmv
-    (M=1 and M=16, 4-bit, N=128256, K=4096) in GB/s against HBM, and the
-    tcgen05 prefill qmm (4-bit, N=14336, K=4096, M=2048 and 8192, bf16
-    result) in TFLOP/s against the dense bf16 peak."""
+    (M=1 and M=16, 4-bit, N=128256, K=4096) in GB/s against HBM, and the two
+    tcgen05 prefill qmms (4-bit, N=14336, K=4096, M=2048 and 8192) in TFLOP/s
+    against the dense bf16 peak: the reassociated one under the default
+    policy with the reference's f32 result, and the bf16-rounding one under
+    the `approximate` policy with a bf16 result."""
     import ctypes
     import torch
     from affon_b200 import _lib
@@ -313,10 +315,12 @@ def kernel_keys(dev, pk):
         N, K = 14336, 4096
         _, sets = make_qmv_operands(dev, 1, N, K, bits, group, copies=1, seed=4)
         w, sc, b = sets[0]
-        for M in (2048, 8192):
+        for M, yd, policy, key in ((2048, "f32", "backend_equivalent", "qmm_exact"),
+                                   (8192, "f32", "backend_equivalent", "qmm_exact"),
+                                   (2048, "bf16", "approximate", "qmm_tc"), (8192, "bf16", "approximate", "qmm_tc")):
             xm = torch.randn((M, K), device=dev).to(torch.bfloat16)
-            y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-            d = _qmm_desc(M, N, K, bits, group, "bf16")
+            y = torch.empty((M, N), dtype=torch.float32 if yd == "f32" else torch.bfloat16, device=dev)
+            d = _qmm_desc(M, N, K, bits, group, yd, policy)
             sel = _lib.Selection()
             check(L.affon_b200_ctx_set_stream(ctx, torch.cuda.current_stream(dev).cuda_stream))
             check(L.affon_b200_qmm_explain(ctx, ctypes.byref(d), xm.data_ptr(), w.data_ptr(), sc.data_ptr(),
@@ -328,23 +332,24 @@ def kernel_keys(dev, pk):
                                        b.data_ptr(), y.data_ptr()))
             ms = _graph_time_ms(launch, 5, dev)
             tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-            out[f"qmm_tc_m{M}_n{N}_k{K}_b4"] = {
+            out[f"{key}_m{M}_n{N}_k{K}_b4"] = {
                 "TFLOP/s": round(tf, 1), "frac_of_measured_bf16": round(tf / pk["bf16_tflops"], 4),
                 "ms_per_launch": round(ms, 4), "implementation": sel.implementation_id.decode(),
-                "shape": f"M={M} N={N} K={K} 4-bit g64, bf16 result"}
+                "shape": f"M={M} N={N} K={K} 4-bit g64, {yd} result, {policy} policy"}
             del xm, y
     finally:
         L.affon_b200_ctx_destroy(ctx)
     return out
 
 
-def _qmm_desc(M, N, K, bits, group, yd):
+def _qmm_desc(M, N, K, bits, group, yd, policy="backend_equivalent"):
     import ctypes
     from affon_b200 import _lib
     per = 32 // bits
     d = _lib.QmmDesc()
     d.struct_size = ctypes.sizeof(_lib.QmmDesc)
     d.bits, d.group_size = bits, group
+    d.numerical_policy = _lib.POLICY[policy]
     d.x_dtype = d.param_dtype = _lib.BF16
     d.y_dtype = _lib.F32 if yd == "f32" else _lib.BF16
     d.x = _lib.View(M, K, K, 1, 0)
@@ -680,18 +685,22 @@ def run_kernel(args, dev):
     check(L.affon_b200_ctx_create(dev.index, None, ctypes.byref(ctx)))
     check(L.affon_b200_ctx_set_stream(ctx, torch.cuda.current_stream(dev).cuda_stream))
     try:
-        if args.kernel == "qmm":
+        if args.kernel in ("qmm", "qmm_exact"):
             M, N, K, bits = 2048, 4096, 4096, 4
             _, sets = make_qmv_operands(dev, 1, N, K, bits, 64, copies=1, seed=4)
             w, sc, b = sets[0]
             xm = torch.randn((M, K), device=dev).to(torch.bfloat16)
-            y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-            d = _qmm_desc(M, N, K, bits, 64, "bf16")
+            exact = args.kernel == "qmm_exact"
+            y = torch.empty((M, N), dtype=torch.float32 if exact else torch.bfloat16, device=dev)
+            d = _qmm_desc(M, N, K, bits, 64, "f32" if exact else "bf16",
+                          "backend_equivalent" if exact else "approximate")
             ms = _timed_launches(lambda: check(L.affon_b200_qmm(ctx, ctypes.byref(d), xm.data_ptr(), w.data_ptr(),
                                                                 sc.data_ptr(), b.data_ptr(), y.data_ptr())),
                                  args.warmup, args.steps, dev)
             tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-            print(json.dumps({"kernel": "qmm", "case": f"M={M} N={N} K={K} 4-bit, bf16 result",
+            case = (f"M={M} N={N} K={K} 4-bit, f32 result, reassociated" if exact else
+                    f"M={M} N={N} K={K} 4-bit, bf16 result, approximate")
+            print(json.dumps({"kernel": args.kernel, "case": case,
                               "ms_per_launch": round(ms, 4), "TFLOP/s": round(tf, 1),
                               "frac_of_measured_bf16": round(tf / pk["bf16_tflops"], 4)}))
             return 0
@@ -849,7 +858,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="affon_b200", choices=["affon_b200", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "qmv", "kernel", "sweep"])
-    ap.add_argument("--kernel", default="gate_up", choices=sorted(KERNEL_CASES) + ["attn", "qmm"],
+    ap.add_argument("--kernel", default="gate_up", choices=sorted(KERNEL_CASES) + ["attn", "qmm", "qmm_exact"],
                     help="--workload kernel: which kernel to run alone")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-keys", action="store_true", help="skip the stand-alone qmv/qmm kernel figures")

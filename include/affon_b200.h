@@ -136,6 +136,13 @@ int affon_b200_ctx_set_overlap(affon_b200_ctx *ctx, int enable);
  * the timeout is reported and the next launch is correct). */
 int affon_b200_debug_set_combine_wait(uint64_t limit_ns, uint32_t extra_arrivals);
 
+/* Test hook of the reassociated prefill qmm, process-wide: the most
+ * activation rows one launch pass takes (rounded down to whole 256-row tiles;
+ * 0 = as many as the workspace holds).  Large M is always processed in row
+ * slices whose group sums fit the workspace; a small cap lets a test run
+ * several slices on a small problem. */
+int affon_b200_debug_set_slice_rows(int64_t rows);
+
 /* Grow the workspace to at least `bytes` (allocates; never called implicitly
  * by a launch, so launches can be captured in CUDA graphs). */
 int affon_b200_ctx_reserve_workspace(affon_b200_ctx *ctx, size_t bytes);

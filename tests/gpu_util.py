@@ -78,3 +78,18 @@ def dense_desc(M, N, K, bits, group=64, xd="bf16", pd="bf16", yd="f32", ldy=None
     d.b = _lib.View(N, K // group, K // group, 1, 0)
     d.y = _lib.View(M, N, ldy or N, 1, 0)
     return d
+
+
+def f64_reference(data, rows=None):
+    """float64 y = x . (codes*s + b)^T for the given weight rows of a
+    synthetic.quantized_linear case, and sum |x||w| (the magnitude a rounding
+    bound scales with)."""
+    from affon_b200 import synthetic
+    x = synthetic.bf16_to_f32(data["x"]).astype(np.float64)
+    r = slice(None) if rows is None else rows
+    g = data.get("group", 64)
+    codes = data["codes"][r].astype(np.float64)
+    s = np.repeat(synthetic.bf16_to_f32(data["s"][r]).astype(np.float64), g, axis=1)
+    b = np.repeat(synthetic.bf16_to_f32(data["b"][r]).astype(np.float64), g, axis=1)
+    w = codes * s + b
+    return x @ w.T, np.abs(x) @ np.abs(w).T

@@ -9,6 +9,7 @@ import pytest
 from affon_b200 import _lib
 from affon_b200.core import AffonError, Tensor, program, qmm_desc_from_specs
 from affon_b200.ops import quantized_matmul, validate_quantized_matmul
+from gpu_util import dense_desc
 
 
 def declared_functions():
@@ -149,3 +150,22 @@ def test_cyna_signature_rejects_bad_shapes_without_gpu():
     assert L.affon_b200_compute_core_run_quantized_matmul_f32(p(f), 16, p(w), 6, p(f), 6, p(f), 6, p(out), 6, 2, 8, 3,
                                                               8, 0) == 1
     assert (out == -1).all()
+
+
+def test_prefill_selection_by_rows_and_policy():
+    """M >= 64 with the default policy selects the reassociated kernel; M = 63
+    stays on qmv passes; `approximate` selects the bf16-rounding kernel;
+    `exact_only` rejects every quantized candidate."""
+    L = _lib.lib()
+    for M, policy, want in [(64, "backend_equivalent", "exact_b4"), (63, "backend_equivalent", "qmv_b4"),
+                            (512, "approximate", "tcgen05_b4"), (4096, "backend_equivalent", "exact_b4")]:
+        d = dense_desc(M, 4096, 4096, 4)
+        d.numerical_policy = _lib.POLICY[policy]
+        sel = _lib.Selection()
+        assert L.affon_b200_select(d, sel) == 0, _lib.last_error()
+        impl = sel.implementation_id.decode()
+        assert impl.endswith(want + "_g64"), (M, policy, impl)
+        assert sel.numerical_class == (2 if policy == "approximate" else 1)
+    d = dense_desc(512, 4096, 4096, 4)
+    d.numerical_policy = _lib.POLICY["exact_only"]
+    assert L.affon_b200_select(d, _lib.Selection()) != 0

@@ -138,11 +138,13 @@ def test_split_k_is_deterministic(ctx):
     assert torch.equal(y1, y2)
 
 
-@pytest.mark.parametrize("M", [17, 33, 64, 100])
+@pytest.mark.parametrize("M", [17, 33, 63, 64, 100])
 def test_qmv_multi_pass(ctx, M):
+    """M > 32 below 64 runs qmv passes over 32-row slices; from 64 rows the
+    reassociated tcgen05 qmm takes over; both within the same gate."""
     data = synthetic.quantized_linear(M, 1024, 4096, bits=4, seed=5)
     y, sel = _run_dense(ctx, data, _upload(ctx, data))
-    assert "qmv" in sel.implementation_id.decode()
+    assert ("qmv" if M < 64 else "qmm_tcgen05_exact") in sel.implementation_id.decode()
     ref = _oracle_rows_f64(data, np.arange(1024))
     assert np.abs(y.cpu().numpy() - ref).max() <= 1e-5 * max(1, np.abs(ref).max())
 

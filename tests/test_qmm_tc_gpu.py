@@ -1,11 +1,12 @@
-"""Prefill qmm on tcgen05 (M >= 64) through the C ABI against the CPU oracle."""
+"""Prefill qmm on tcgen05 with bf16-rounded decoded weights (the
+`approximate` policy, M >= 64) through the C ABI against the CPU oracle."""
 import numpy as np
 import pytest
 import torch
 
 import oracle
 from affon_b200 import _lib, synthetic
-from gpu_util import Ctx, dense_desc
+from gpu_util import Ctx, dense_desc, f64_reference as _f64
 
 pytestmark = pytest.mark.gpu
 
@@ -17,7 +18,10 @@ def ctx():
     c.close()
 
 
-def _run(ctx, data, yd="bf16", policy="backend_equivalent"):
+APPROX = "cuda_quantized_matmul.sm100_qmm_tcgen05_b{}_g64"
+
+
+def _run(ctx, data, yd="bf16", policy="approximate"):
     M, N, K, bits = data["M"], data["N"], data["K"], data["bits"]
     dev = ctx.device
     up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int32 if a.dtype == np.uint32 else np.int16)).to(dev)
@@ -28,16 +32,6 @@ def _run(ctx, data, yd="bf16", policy="backend_equivalent"):
     sel = ctx.qmm(d, x.data_ptr(), w.data_ptr(), s.data_ptr(), b.data_ptr(), y.data_ptr())
     assert _lib.lib().affon_b200_ctx_synchronize(ctx.ptr) == 0, _lib.last_error()
     return y.float().cpu().numpy().astype(np.float64), sel.implementation_id.decode()
-
-
-def _f64(data, rows=None):
-    x = synthetic.bf16_to_f32(data["x"]).astype(np.float64)
-    r = slice(None) if rows is None else rows
-    codes = data["codes"][r].astype(np.float64)
-    s = np.repeat(synthetic.bf16_to_f32(data["s"][r]).astype(np.float64), 64, axis=1)
-    b = np.repeat(synthetic.bf16_to_f32(data["b"][r]).astype(np.float64), 64, axis=1)
-    w = codes * s + b
-    return x @ w.T, np.abs(x) @ np.abs(w).T
 
 
 @pytest.mark.parametrize("bits", [4, 8])
@@ -55,7 +49,7 @@ def test_qmm_tc_exact_when_weights_are_bf16_exact(ctx, bits, M, N, K):
     data["s"] = synthetic.bf16_round_bits(s)
     data["b"] = synthetic.bf16_round_bits(-(1 << (bits - 1)) * s)
     y, impl = _run(ctx, data, "f32", "approximate")
-    assert "qmm_tcgen05" in impl, impl
+    assert impl == APPROX.format(bits), impl
     ref = oracle.qmm_dense(data["x"], "bf16", data["w"], data["s"], data["b"], "bf16", M, N, K, bits, 64,
                            threads=oracle.cpu_threads())
     np.testing.assert_array_equal(y, ref.astype(np.float64))
@@ -71,11 +65,11 @@ def test_qmm_tc_baseline_distributions(ctx, bits, M, N, K):
     rows = np.arange(N) if N <= 1024 else np.linspace(0, N - 1, 1024).astype(np.int64)
     ref, mag = _f64(data, rows)
     y16, impl = _run(ctx, data, "bf16")
-    assert "qmm_tcgen05" in impl, impl
+    assert impl == APPROX.format(bits), impl
     peak = max(1.0, np.abs(ref).max())
     assert np.abs(y16[:, rows] - ref).max() / peak <= 2e-2
     y32, impl = _run(ctx, data, "f32", "approximate")
-    assert "qmm_tcgen05" in impl
+    assert impl == APPROX.format(bits)
     assert (np.abs(y32[:, rows] - ref) <= 2.0 ** -8 * mag + 1e-6).all()
 
 
@@ -87,7 +81,7 @@ def test_qmm_tc_m8192(ctx, N):
     M, K = 8192, 4096
     data = synthetic.quantized_linear(M, N, K, bits=4, seed=3)
     y, impl = _run(ctx, data, "bf16")
-    assert "qmm_tcgen05" in impl, impl
+    assert impl == APPROX.format(4), impl
     assert np.isfinite(y).all()
     rows = np.linspace(0, N - 1, 256).astype(np.int64)
     ref, _ = _f64(data, rows)
@@ -101,7 +95,7 @@ def test_qmm_tc_large_property(ctx):
     M, N, K = 2048, 128256, 4096
     data = synthetic.quantized_linear(M, N, K, bits=4, seed=1)
     y, impl = _run(ctx, data, "bf16")
-    assert "qmm_tcgen05" in impl
+    assert impl == APPROX.format(4), impl
     assert np.isfinite(y).all()
     rows = np.linspace(0, N - 1, 256).astype(np.int64)
     ref, _ = _f64(data, rows)
@@ -131,7 +125,7 @@ def test_qmm_tc_repeated_runs_are_identical_and_bounded(ctx, bits):
     first = None
     for _ in range(5):
         y, impl = _run(ctx, data, "f32", "approximate")
-        assert "qmm_tcgen05" in impl
+        assert impl == APPROX.format(bits), impl
         assert (np.abs(y - ref) <= 2.0 ** -8 * mag + 1e-6).all()
         if first is None:
             first = y
