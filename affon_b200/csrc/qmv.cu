@@ -173,9 +173,10 @@ __device__ __forceinline__ int pair_slot(int e) { return (e < 4) ? 2 * e : 2 * (
 // Residual update of one element: h += v, the next projection's
 // activation bf16(h * gamma_next) at its column-order position when asked,
 // and the square for the sums of squares.
-__device__ __forceinline__ float resid_update(const Params &p, int m, int64_t n, float v, float &ssq) {
+__device__ __forceinline__ float resid_update(const Params &p, int m, int64_t n, float v, float &ssq,
+                                              const float *h_pre = nullptr) {
     float *h = p.f.h_out + m * p.f.ld_h_out;
-    const float hv = h[n] + v;
+    const float hv = (h_pre ? *h_pre : h[n]) + v;
     h[n] = hv;
     if (p.f.next_x) {
         const int e = static_cast<int>(n & 7);
@@ -308,9 +309,10 @@ __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT
 // n+8 sit in lanes l and l+8).  Called by all 32 lanes with the same m.
 // Residual update of rows n (one per lane, 32 consecutive rows per warp,
 // the same m) with the per-16-row sums of squares.  Called by all 32 lanes.
-__device__ __forceinline__ void resid_row(const Params &p, int m, int64_t n, float v, int lane, bool ok) {
+__device__ __forceinline__ void resid_row(const Params &p, int m, int64_t n, float v, int lane, bool ok,
+                                          const float *h_pre = nullptr) {
     float ssq = 0.0f;
-    if (ok) resid_update(p, m, n, v, ssq);
+    if (ok) resid_update(p, m, n, v, ssq, h_pre);
     ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
     ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
     ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
@@ -319,12 +321,12 @@ __device__ __forceinline__ void resid_row(const Params &p, int m, int64_t n, flo
 }
 
 __device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, float v, int lane, bool active,
-                                           const float *rs) {
+                                           const float *rs, const float *h_pre = nullptr) {
     const bool ok = active && n < p.N;
     if (rs) v *= rs[m];
     switch (p.f.epi) {
     case EPI_RESID:
-        resid_row(p, m, n, v, lane, ok);
+        resid_row(p, m, n, v, lane, ok, h_pre);
         break;
     case EPI_RESID_AR:
         if (ok) ar_push(p, m, n, v);
@@ -370,13 +372,15 @@ __device__ __forceinline__ void block_contributors(const Params &p, int blk, int
 // written its slot.
 template <int MT, int NT, int CW>
 __device__ __forceinline__ void segment_epilogue(const Params &p, const float (&acc)[NT][MT][4], int blk, int warp,
-                                                 int g, int t, int tid, const float *rs) {
+                                                 int g, int t, int tid, const float *rs, uint64_t *rsbar,
+                                                 volatile int *abort) {
     constexpr int CT = CW * 32;  // consumer threads
     constexpr int ROWS = 16 * NT * CW;
     int first, total;
     block_contributors(p, blk, first, total);
     const int64_t nb0 = static_cast<int64_t>(blk) * ROWS;
     if (total == 1) {
+        if (rs) mbar_wait(rsbar, 0, abort, p.status);  // the row scales are out
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) finish_tile<MT>(p, acc[nt], nb0 + (warp * NT + nt) * 16, g, t, rs);
         if (p.f.epi == EPI_RESID_AR) ar_signal<CW>(p, blk * p.max_slots, tid);
@@ -408,29 +412,59 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *a) {
     return v;
 }
 
-// Second phase (every CTA of the grid is resident): for each block this CTA
-// contributed to, wait until all its contributors have published their
-// slots, then sum the slots in slot order for this CTA's share of the
-// block's 16-row tiles and apply the epilogue.  The CTA finishing last resets
-// the block's counters for the next launch.  The wait is bounded; on timeout
-// the status word says TIMEOUT and the CTA goes on (its results are then
-// garbage, and the counters are still reset).
+// One block this CTA shares with other contributors: its slot and this
+// CTA's share of the block's 16-row tiles.
+struct SharedBlock {
+    int blk, slot, total, row0, nrows, units;
+};
+
+template <int ROWS>
+__device__ __forceinline__ SharedBlock shared_block(const Params &p, int blk) {
+    constexpr int TILES = ROWS / 16;
+    SharedBlock b;
+    int first;
+    block_contributors(p, blk, first, b.total);
+    b.blk = blk;
+    b.slot = static_cast<int>(blockIdx.x) - first;
+    const int t0 = b.slot * TILES / b.total, t1 = (b.slot + 1) * TILES / b.total;
+    b.row0 = t0 * 16;
+    b.nrows = (t1 - t0) * 16;
+    b.units = ((b.nrows + 31) / 32) * p.M;
+    return b;
+}
+
+// Second phase (every CTA of the grid is resident).  Only the first and the
+// last block of a CTA's range can be shared with other CTAs (every block in
+// between lies inside the range).  For those, wait until all contributors
+// have published their slots, then sum the slots in slot order for this
+// CTA's share of each block's 16-row tiles and apply the epilogue -- both
+// blocks in one pass, so their slot loads travel together.  The CTA finishing
+// a block last resets its counters for the next launch.  The waits are
+// bounded; on timeout the status word says TIMEOUT and the CTA goes on (its
+// results are then garbage, and the counters are still reset).
 template <int ROWS, int CW>
 __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp, int lane, int tid,
-                               volatile int *abort, const float *rs) {
-    constexpr int CT = CW * 32, TILES = ROWS / 16, UB = 4, MAXS = 4;
+                               volatile int *abort, const float *rs, uint64_t *rsbar) {
+    // Units per batch: eight where the 168-register variants have room, four
+    // in the 128-register ones.
+    constexpr int CT = CW * 32, UB = CW == 12 ? 4 : 8, MAXS = 4;
     if (hi <= lo) return;
     unsigned *done = p.counters + kMaxTiles / 2;
     const int b_first = static_cast<int>(lo / p.spb), b_last = static_cast<int>((hi - 1) / p.spb);
-    for (int blk = b_first; blk <= b_last; ++blk) {
-        int first, total;
-        block_contributors(p, blk, first, total);
-        if (total == 1) continue;
-        const int slot = static_cast<int>(blockIdx.x) - first;
-        if (tid == 0) {
-            const unsigned want = static_cast<unsigned>(total) + p.extra_arrivals;
-            const uint64_t start = globaltimer();
-            while (ld_acquire_gpu(&p.counters[blk]) < want) {
+    SharedBlock A = shared_block<ROWS>(p, b_first), B = shared_block<ROWS>(p, b_last);
+    const bool hasA = A.total > 1, hasB = b_last != b_first && B.total > 1;
+    if (!hasA && !hasB) return;
+    if (!hasA) {  // B alone: keep it in the first place
+        A = B;
+    }
+    const bool two = hasA && hasB;
+    if (!two) B.units = 0;
+    if (tid == 0) {
+        const uint64_t start = globaltimer();
+        for (int k = 0; k < (two ? 2 : 1); ++k) {
+            const SharedBlock &sb = k == 0 ? A : B;
+            const unsigned want = static_cast<unsigned>(sb.total) + p.extra_arrivals;
+            while (ld_acquire_gpu(&p.counters[sb.blk]) < want) {
                 if (*abort || globaltimer() - start > p.arrival_wait_ns) {
                     *abort = 1;
                     atomicExch(p.status, static_cast<unsigned>(DEV_TIMEOUT));
@@ -439,52 +473,60 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
                 __nanosleep(64);
             }
         }
-        named_bar_sync(1, CT);
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        const float *base = p.partial + static_cast<int64_t>(blk) * p.max_slots * p.M * ROWS;
-        const int t0 = slot * TILES / total, t1 = (slot + 1) * TILES / total;
-        const int row0 = t0 * 16, nrows = (t1 - t0) * 16;
-        const int chunks = (nrows + 31) / 32;
-        const int units = chunks * p.M;
-        const int64_t slot_stride = static_cast<int64_t>(p.M) * ROWS;
-        // Work unit = (32-row chunk, activation row m), one warp each; a warp
-        // takes UB units at a time and issues every slot load of all of them
-        // before summing, so the combine costs about one L2 round trip per
-        // batch instead of one per unit.
-        for (int ub = warp; ub < units; ub += CW * UB) {
-            float part[UB][MAXS];
+    }
+    named_bar_sync(1, CT);
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    if (rs) mbar_wait(rsbar, 0, abort, p.status);  // the row scales are out
+    const int64_t slot_stride = static_cast<int64_t>(p.M) * ROWS;
+    const float *baseA = p.partial + static_cast<int64_t>(A.blk) * p.max_slots * slot_stride;
+    const float *baseB = p.partial + static_cast<int64_t>(B.blk) * p.max_slots * slot_stride;
+    const int units = A.units + B.units;
+    // Work unit = (block, 32-row chunk, activation row m), one warp each; a
+    // warp takes UB units at a time and issues every slot load of all of them
+    // before summing, so the combine costs about one L2 round trip per batch.
+    for (int ub = warp; ub < units; ub += CW * UB) {
+        float part[UB][MAXS];
 #pragma unroll
-            for (int u = 0; u < UB; ++u) {
-                const int unit = ub + u * CW;
-                const int uu = unit < units ? unit : 0;
-                const int chunk = uu / p.M, m = uu - chunk * p.M;
-                const int rr = chunk * 32 + lane;
-                const int row = row0 + (rr < nrows ? rr : 0);
-                const float *src = base + static_cast<int64_t>(m) * ROWS + row;
+        for (int u = 0; u < UB; ++u) {
+            const int unit = ub + u * CW;
+            const bool inB = unit >= A.units;
+            const int local = unit < units ? (inB ? unit - A.units : unit) : 0;
+            const int chunk = local / p.M, m = local - chunk * p.M;
+            const int rr = chunk * 32 + lane;
+            const int nrows = inB ? B.nrows : A.nrows, total = inB ? B.total : A.total;
+            const int row = (inB ? B.row0 : A.row0) + (rr < nrows ? rr : 0);
+            const float *src = (inB ? baseB : baseA) + static_cast<int64_t>(m) * ROWS + row;
 #pragma unroll
-                for (int k = 0; k < MAXS; ++k) part[u][k] = (k < total && unit < units) ? __ldcg(src + k * slot_stride) : 0.0f;
-            }
-            // Slots beyond MAXS (more than MAXS contributors) are added after.
-#pragma unroll
-            for (int u = 0; u < UB; ++u) {
-                const int unit = ub + u * CW;
-                if (unit >= units) break;  // warp-uniform
-                const int chunk = unit / p.M, m = unit - chunk * p.M;
-                const int rr = chunk * 32 + lane;
-                const bool active = rr < nrows;
-                const int row = row0 + (active ? rr : 0);
-                float v = 0.0f;
-#pragma unroll
-                for (int k = 0; k < MAXS; ++k)
-                    if (k < total) v += part[u][k];
-                for (int k = MAXS; k < total; ++k) v += __ldcg(base + static_cast<int64_t>(m) * ROWS + row + k * slot_stride);
-                finish_row(p, m, static_cast<int64_t>(blk) * ROWS + row0 + rr, v, lane, active, rs);
-            }
+            for (int k = 0; k < MAXS; ++k) part[u][k] = (k < total && unit < units) ? __ldcg(src + k * slot_stride) : 0.0f;
         }
-        if (p.f.epi == EPI_RESID_AR) ar_signal<CW>(p, blk * p.max_slots + slot, tid);
-        if (tid == 0 && atomicAdd(&done[blk], 1u) == static_cast<unsigned>(total - 1)) {
-            p.counters[blk] = 0u;
-            done[blk] = 0u;
+        // Slots beyond MAXS (more than MAXS contributors) are added after.
+#pragma unroll
+        for (int u = 0; u < UB; ++u) {
+            const int unit = ub + u * CW;
+            if (unit >= units) break;  // warp-uniform
+            const bool inB = unit >= A.units;
+            const int local = inB ? unit - A.units : unit;
+            const int chunk = local / p.M, m = local - chunk * p.M;
+            const int rr = chunk * 32 + lane;
+            const int nrows = inB ? B.nrows : A.nrows, total = inB ? B.total : A.total;
+            const int row0 = inB ? B.row0 : A.row0, blk = inB ? B.blk : A.blk;
+            const bool active = rr < nrows;
+            const int row = row0 + (active ? rr : 0);
+            const float *src = (inB ? baseB : baseA) + static_cast<int64_t>(m) * ROWS + row;
+            float v = 0.0f;
+#pragma unroll
+            for (int k = 0; k < MAXS; ++k)
+                if (k < total) v += part[u][k];
+            for (int k = MAXS; k < total; ++k) v += __ldcg(src + k * slot_stride);
+            finish_row(p, m, static_cast<int64_t>(blk) * ROWS + row0 + rr, v, lane, active, rs);
+        }
+    }
+    for (int k = 0; k < (two ? 2 : 1); ++k) {
+        const SharedBlock &sb = k == 0 ? A : B;
+        if (p.f.epi == EPI_RESID_AR) ar_signal<CW>(p, sb.blk * p.max_slots + sb.slot, tid);
+        if (tid == 0 && atomicAdd(&done[sb.blk], 1u) == static_cast<unsigned>(sb.total - 1)) {
+            p.counters[sb.blk] = 0u;
+            done[sb.blk] = 0u;
         }
     }
 }
@@ -527,20 +569,36 @@ __device__ void ar_finish(const Params &p, int64_t lo, int64_t hi, int warp, int
         const int t0 = total == 1 ? 0 : slot * TILES / total, t1 = total == 1 ? TILES : (slot + 1) * TILES / total;
         const int row0 = t0 * 16, nrows = (t1 - t0) * 16;
         const int units = ((nrows + 31) / 32) * p.M;
-        for (int u = warp; u < units; u += CW) {
-            const int chunk = u / p.M, m = u - chunk * p.M;
-            const int rr = chunk * 32 + lane;
-            const int64_t n = static_cast<int64_t>(blk) * ROWS + row0 + rr;
-            const bool ok = rr < nrows && n < p.N;
-            float part[kTpMaxWorld];
+        constexpr int AUB = CW == 12 ? 2 : 4;  // units whose loads travel together
+        for (int u0 = warp; u0 < units; u0 += CW * AUB) {
+            float part[AUB][kTpMaxWorld], hpre[AUB];
 #pragma unroll
-            for (int r = 0; r < kTpMaxWorld; ++r)
-                part[r] = (ok && r < p.f.tp_world) ? __ldcg(recv + r * src_stride + static_cast<int64_t>(m) * p.N + n) : 0.0f;
-            float v = 0.0f;
+            for (int k = 0; k < AUB; ++k) {
+                const int u = u0 + k * CW;
+                const int chunk = u / p.M, m = u - chunk * p.M;
+                const int rr = chunk * 32 + lane;
+                const int64_t n = static_cast<int64_t>(blk) * ROWS + row0 + rr;
+                const bool ok = u < units && rr < nrows && n < p.N;
 #pragma unroll
-            for (int r = 0; r < kTpMaxWorld; ++r)
-                if (r < p.f.tp_world) v += part[r];
-            resid_row(p, m, n, v, lane, ok);
+                for (int r = 0; r < kTpMaxWorld; ++r)
+                    part[k][r] = (ok && r < p.f.tp_world) ? __ldcg(recv + r * src_stride + static_cast<int64_t>(m) * p.N + n)
+                                                         : 0.0f;
+                hpre[k] = ok ? p.f.h_out[m * p.f.ld_h_out + n] : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < AUB; ++k) {
+                const int u = u0 + k * CW;
+                if (u >= units) break;  // warp-uniform
+                const int chunk = u / p.M, m = u - chunk * p.M;
+                const int rr = chunk * 32 + lane;
+                const int64_t n = static_cast<int64_t>(blk) * ROWS + row0 + rr;
+                const bool ok = rr < nrows && n < p.N;
+                float v = 0.0f;
+#pragma unroll
+                for (int r = 0; r < kTpMaxWorld; ++r)
+                    if (r < p.f.tp_world) v += part[k][r];
+                resid_row(p, m, n, v, lane, ok, &hpre[k]);
+            }
         }
     }
 }
@@ -561,6 +619,7 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
     uint64_t *xsfull = empty + MAX_STAGES;
     volatile int *abort = reinterpret_cast<volatile int *>(xsfull + MAX_STAGES);
     __shared__ float s_rscale[MAX_XR];  // RMSNorm row scales (row_scale mode)
+    __shared__ uint64_t s_rsbar;        // completes once s_rscale holds them
     const float *rs = p.f.row_ss ? s_rscale : nullptr;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -572,6 +631,7 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
             mbar_init(&empty[s], CW + 1);  // consumer warps and the sum warp
             mbar_init(&xsfull[s], 1);
         }
+        mbar_init(&s_rsbar, 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -634,42 +694,57 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
         __syncwarp();
     } else if (warp == CW + 1) {  // ----------------------------- group sums
         pdl_wait();
-        if (p.f.row_ss) {
-            // Row scales rsqrt(sum_k h^2 / K + eps) of the unnormalised
-            // activations from their per-16-column sums of squares: lane l
-            // adds tiles l, l + 32, ... for every row at once (one row of 32
-            // floats per tile, all loads in flight), then a butterfly per row
-            // -- the RMSNorm prologue's order.  Published to the consumers by
-            // the first xsfull arrival below.
-            float acc[MAX_XR];
+        // Row scales rsqrt(sum_k h^2 / K + eps) of the unnormalised
+        // activations from their per-16-column sums of squares: lane l adds
+        // tiles l, l + 32, ... for every row (two tiles' loads in flight at a
+        // time), then a butterfly per row -- the RMSNorm prologue's order.
+        // Only the epilogues use them, so they are formed once the first ring
+        // fill's group sums are out, while the consumers work on those stages,
+        // and published through s_rsbar.
+        auto row_scales = [&]() {
+            constexpr int RMAX = 8 * MT;  // activation rows this instantiation serves
+            float acc[RMAX];
 #pragma unroll
-            for (int m = 0; m < MAX_XR; ++m) acc[m] = 0.0f;
-            for (int tl = lane; tl < p.f.ss_tiles; tl += 32) {
-                const float4 *row = reinterpret_cast<const float4 *>(p.f.row_ss + tl * kSsWidth);
+            for (int m = 0; m < RMAX; ++m) acc[m] = 0.0f;
+            const int quads = (p.M + 3) / 4;
+            for (int tl0 = lane; tl0 < p.f.ss_tiles; tl0 += 64) {
+                float4 v[2][RMAX / 4];
 #pragma unroll
-                for (int q = 0; q < MAX_XR / 4; ++q) {
-                    const float4 v = __ldcg(row + q);
-                    acc[4 * q] += v.x;
-                    acc[4 * q + 1] += v.y;
-                    acc[4 * q + 2] += v.z;
-                    acc[4 * q + 3] += v.w;
+                for (int j = 0; j < 2; ++j) {
+                    const int tl = tl0 + 32 * j;
+                    const float4 *row = reinterpret_cast<const float4 *>(p.f.row_ss + tl * kSsWidth);
+#pragma unroll
+                    for (int q = 0; q < RMAX / 4; ++q)
+                        v[j][q] = (tl < p.f.ss_tiles && q < quads) ? __ldcg(row + q) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int q = 0; q < RMAX / 4; ++q) {
+                        acc[4 * q] += v[j][q].x;
+                        acc[4 * q + 1] += v[j][q].y;
+                        acc[4 * q + 2] += v[j][q].z;
+                        acc[4 * q + 3] += v[j][q].w;
+                    }
             }
 #pragma unroll
-            for (int m = 0; m < MAX_XR; ++m) {
+            for (int m = 0; m < RMAX; ++m) {
                 float sum = acc[m];
 #pragma unroll
                 for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
                 if (lane == 0 && m < p.M) s_rscale[m] = rsqrtf(sum / static_cast<float>(p.K) + p.f.eps);
             }
             __syncwarp();
-        }
+            if (lane == 0) mbar_arrive(&s_rsbar);
+        };
+        const int64_t first_fill = lo + S < hi ? lo + S : hi;
         // X_g = sum_{k in g} x[m][k] for every activation row, once per CTA and
         // stage, via m16n8k16 MMAs with an all-ones A operand (rows equal).
         const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 1.0 pairs
         int stage = 0;
         uint32_t phase = 0;
         for (int64_t i = lo; i < hi; ++i) {
+            if (p.f.row_ss && i == first_fill) row_scales();
             mbar_wait(&full[stage], phase, abort, p.status);
             const char *xsb = ring + stage * Sh::BYTES + Sh::W + 2 * Sh::SB;
             float *xs = xsums + stage * GPS * MAX_XR;
@@ -698,6 +773,7 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
             }
             if (++stage == S) { stage = 0; phase ^= 1; }
         }
+        if (p.f.row_ss && first_fill == hi) row_scales();  // a range no longer than the ring
     } else {  // ------------------------------------------------- consumers
         pdl_wait();
         int stage = 0;
@@ -850,9 +926,9 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
                     accf[nt][mt][2] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][1]));
                     accf[nt][mt][3] = __uint_as_float(static_cast<uint32_t>(acc[nt][mt][1] >> 32));
                 }
-            segment_epilogue<MT, NT, CW>(p, accf, blk, warp, g, t, tid, rs);
+            segment_epilogue<MT, NT, CW>(p, accf, blk, warp, g, t, tid, rs, &s_rsbar, abort);
         }
-        combine_blocks<ROWS, CW>(p, lo, hi, warp, lane, tid, abort, rs);
+        combine_blocks<ROWS, CW>(p, lo, hi, warp, lane, tid, abort, rs, &s_rsbar);
         if (p.f.epi == EPI_RESID_AR) ar_finish<ROWS, CW>(p, lo, hi, warp, lane, tid, abort);
     }
 }
