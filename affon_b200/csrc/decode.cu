@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_attention_kernel(const __gr
         if (lane == 0 && t1 > t0) {
             tma_prefetch_desc(&kmap);
             tma_prefetch_desc(&vmap);
+            const uint64_t stream_policy = l2_evict_first();
             int stage = 0;
             uint32_t phase = 0, issued = 0, par = 0;
             for (int i = t0; i < t1; ++i) {
@@ -122,10 +123,10 @@ __global__ void __launch_bounds__(THREADS, 2) decode_attention_kernel(const __gr
                 char *dst = ring + stage * STAGE_BYTES;
                 mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
                 const int row = static_cast<int>(row_base) + i * TILE;
-                tma_load_2d(dst, &kmap, &full[stage], 0, row);
-                tma_load_2d(dst + BOX, &kmap, &full[stage], 64, row);
-                tma_load_2d(dst + 2 * BOX, &vmap, &full[stage], 0, row);
-                tma_load_2d(dst + 3 * BOX, &vmap, &full[stage], 64, row);
+                tma_load_2d_hint(dst, &kmap, &full[stage], 0, row, stream_policy);
+                tma_load_2d_hint(dst + BOX, &kmap, &full[stage], 64, row, stream_policy);
+                tma_load_2d_hint(dst + 2 * BOX, &vmap, &full[stage], 0, row, stream_policy);
+                tma_load_2d_hint(dst + 3 * BOX, &vmap, &full[stage], 64, row, stream_policy);
                 issued |= 1u << stage;
                 par = (par & ~(1u << stage)) | (phase << stage);
                 if (++stage == STAGES) { stage = 0; phase ^= 1; }

@@ -648,6 +648,7 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
             tma_prefetch_desc(&smap);
             tma_prefetch_desc(&bmap);
             tma_prefetch_desc(&xmap);
+            const uint64_t stream_policy = l2_evict_first();
             auto load_params = [&](int stage, int64_t i) {
                 const int blk = static_cast<int>(i / p.spb), st = static_cast<int>(i - int64_t(blk) * p.spb);
                 char *dst = ring + stage * Sh::BYTES;
@@ -657,9 +658,10 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
 #pragma unroll
                 for (int bx = 0; bx < ROWS / BOX_ROWS; ++bx) {
                     const int row0 = blk * ROWS + bx * BOX_ROWS;
-                    tma_load_2d(dst + bx * BOX_ROWS * 128, &wmap, &full[stage], kk * BITS / 32, row0);
-                    tma_load_2d(dst + Sh::W + bx * BOX_ROWS * 16, &smap, &full[stage], g8, row0);
-                    tma_load_2d(dst + Sh::W + Sh::SB + bx * BOX_ROWS * 16, &bmap, &full[stage], g8, row0);
+                    tma_load_2d_hint(dst + bx * BOX_ROWS * 128, &wmap, &full[stage], kk * BITS / 32, row0, stream_policy);
+                    tma_load_2d_hint(dst + Sh::W + bx * BOX_ROWS * 16, &smap, &full[stage], g8, row0, stream_policy);
+                    tma_load_2d_hint(dst + Sh::W + Sh::SB + bx * BOX_ROWS * 16, &bmap, &full[stage], g8, row0,
+                                     stream_policy);
                 }
             };
             auto load_x = [&](int stage, int64_t i) {

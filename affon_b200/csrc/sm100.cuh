@@ -94,6 +94,24 @@ AFB_DEVICE void tma_load_2d(void *smem_dst, const CUtensorMap *map, uint64_t *ba
         ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
 }
+// The same load with an L2 cache policy (e.g. l2_evict_first()).
+AFB_DEVICE void tma_load_2d_hint(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1,
+                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1),
+        "l"(policy)
+        : "memory");
+}
+// L2 policy for data read once per launch (streamed weights, caches): its
+// lines are the first evicted, so streaming does not push out what the
+// surrounding kernels reuse.
+AFB_DEVICE uint64_t l2_evict_first() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
 AFB_DEVICE void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
