@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_attention_kernel(const __gr
             int stage = 0;
             uint32_t phase = 0, issued = 0, par = 0;
             for (int i = t0; i < t1; ++i) {
-                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) break;
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status) || *abort) break;  // never re-arm after an abort
                 char *dst = ring + stage * STAGE_BYTES;
                 mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
                 const int row = static_cast<int>(row_base) + i * TILE;

@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
                 const int mb = t % p.m_blocks;
                 for (int st = 0; st < SPT; ++st) {
-                    if (mbar_wait(&xempty[s], ph ^ 1, abort, p.status)) {
+                    if (mbar_wait(&xempty[s], ph ^ 1, abort, p.status) && !*abort) {  // never re-arm after an abort
                         mbar_arrive_expect_tx(&xfull[s], X_BYTES);
                         if (st < G)
                             tma_load_2d(xs + s * X_BYTES, &xmap, &xfull[s], st * BK, mb * BX);
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
                 const int nb = t / p.m_blocks;
                 for (int g = 0; g < G; ++g) {
-                    if (mbar_wait(&pempty[s], ph ^ 1, abort, p.status)) {
+                    if (mbar_wait(&pempty[s], ph ^ 1, abort, p.status) && !*abort) {
                         mbar_arrive_expect_tx(&pfull[s], C::P_BYTES);
                         tma_load_2d(ps + s * C::P_BYTES, &wmap, &pfull[s], g * (BK * BITS / 32), nb * BW);
                         issued |= 1u << s;

@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
                 const int mb = t % p.m_blocks;
                 for (int kb = 0; kb < KB; ++kb) {
-                    if (mbar_wait(&sempty[s], ph ^ 1, abort, p.status)) {
+                    if (mbar_wait(&sempty[s], ph ^ 1, abort, p.status) && !*abort) {  // never re-arm after an abort
                         mbar_arrive_expect_tx(&xfull[s], X_BYTES);
                         tma_load_2d(xs + s * X_BYTES, &xmap, &xfull[s], kb * BK, mb * BX);
                     }
@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
                 const int nb = t / p.m_blocks;
                 for (int kb = 0; kb < KB; ++kb) {
-                    if (mbar_wait(&pempty[s], ph ^ 1, abort, p.status)) {
+                    if (mbar_wait(&pempty[s], ph ^ 1, abort, p.status) && !*abort) {
                         mbar_arrive_expect_tx(&pfull[s], C::P_BYTES);
                         tma_load_2d(ps + s * C::P_BYTES, &wmap, &pfull[s], kb * (BK * BITS / 32), nb * BW);
                     }

@@ -94,18 +94,25 @@ struct Shape {
     static constexpr int GPS = BITS == 4 ? 4 : 2;     // groups per stage (128 packed bytes per row)
     static constexpr int KPS = GPS * GROUP;           // K per stage
     static constexpr int W = ROWS * 128;              // packed bytes per stage
-    static constexpr int SB = ROWS * 16;              // one 8-group box of scales (or biases)
+    static constexpr int SB = (ROWS * 16 + 511) / 512 * 512;  // one 8-group box of scales (or biases), padded
     static constexpr int X = GPS * X_BOX;
     static constexpr int BYTES = W + 2 * SB + X;      // swizzled regions (W, X) stay 1024-byte aligned
+    static constexpr int TX_BYTES = W + 2 * ROWS * 16 + X;  // bytes the stage's TMA loads deliver (no padding)
     static_assert(W % 1024 == 0 && (2 * SB) % 1024 == 0 && X % 1024 == 0 && BOX_ROWS <= 256, "stage layout");
 };
 
 // Instantiations (variant: MT, NT, CW -> block rows): M <= 8: 0 = (1, 2, 12)
 // -> 384, 1 = (1, 1, 12) -> 192; M <= 16: 2 = (2, 2, 10) -> 320, 3 = (2, 1, 10)
-// -> 160; M <= 32: 4 = (4, 1, 10) -> 160.  The planner picks, per shape, the
-// variant with the smallest estimated makespan.
-constexpr int kVariantRows[5] = {384, 192, 320, 160, 160};
-constexpr int kVariantNT[5] = {2, 1, 2, 1, 1};
+// -> 160, 5 = (2, 1, 13) -> 208 (whole-K blocks, one per CTA); M <= 32: 4 =
+// (4, 1, 10) -> 160.  The planner picks, per shape, the variant with the
+// smallest estimated makespan.
+constexpr int kVariantRows[6] = {384, 192, 320, 160, 160, 208};
+constexpr int kVariantNT[6] = {2, 1, 2, 1, 1, 1};
+constexpr int kVariantBoxRows[6] = {192, 192, 160, 160, 160, 208};  // 16 rows per consumer warp
+static_assert(Shape<4, 1, 2, 12>::BOX_ROWS == kVariantBoxRows[0] && Shape<4, 1, 1, 12>::BOX_ROWS == kVariantBoxRows[1] &&
+                  Shape<4, 2, 2, 10>::BOX_ROWS == kVariantBoxRows[2] && Shape<4, 2, 1, 10>::BOX_ROWS == kVariantBoxRows[3] &&
+                  Shape<4, 4, 1, 10>::BOX_ROWS == kVariantBoxRows[4] && Shape<4, 2, 1, 13>::BOX_ROWS == kVariantBoxRows[5],
+              "tensor-map boxes match the kernels' boxes");
 
 struct Params {
     void *y;
@@ -652,7 +659,7 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
             auto load_params = [&](int stage, int64_t i) {
                 const int blk = static_cast<int>(i / p.spb), st = static_cast<int>(i - int64_t(blk) * p.spb);
                 char *dst = ring + stage * Sh::BYTES;
-                mbar_arrive_expect_tx(&full[stage], Sh::BYTES);
+                mbar_arrive_expect_tx(&full[stage], Sh::TX_BYTES);
                 const int kk = st * KPS;
                 const int g8 = (kk / GROUP) & ~7;
 #pragma unroll
@@ -681,8 +688,10 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
             uint32_t issued_mask = (1u << pre) - 1u, issued_par = 0;  // stages 0..pre-1 at parity 0
             for (int64_t i = lo + pre; i < hi; ++i) {
                 // On a timed-out wait (abort set) stop issuing loads; the other
-                // roles walk to the end without waiting.
-                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status)) break;
+                // roles walk to the end without waiting.  A stage is never
+                // re-armed after an abort: a stage whose loads did not all
+                // land has an unfinished phase.
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort, p.status) || *abort) break;
                 load_params(stage, i);
                 load_x(stage, i);
                 issued_mask |= 1u << stage;
@@ -1117,6 +1126,7 @@ int stage_bytes(int bits, int variant) {
     case 1: return bits == 4 ? qmv::Shape<4, 1, 1, 12>::BYTES : qmv::Shape<8, 1, 1, 12>::BYTES;
     case 2: return bits == 4 ? qmv::Shape<4, 2, 2, 10>::BYTES : qmv::Shape<8, 2, 2, 10>::BYTES;
     case 3: return bits == 4 ? qmv::Shape<4, 2, 1, 10>::BYTES : qmv::Shape<8, 2, 1, 10>::BYTES;
+    case 5: return bits == 4 ? qmv::Shape<4, 2, 1, 13>::BYTES : qmv::Shape<8, 2, 1, 13>::BYTES;
     default: return bits == 4 ? qmv::Shape<4, 4, 1, 10>::BYTES : qmv::Shape<8, 4, 1, 10>::BYTES;
     }
 }
@@ -1128,12 +1138,13 @@ QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     // row-stages (items per CTA x block rows), with one-tile-per-warp variants
     // charged 12% for their lower activation-fragment reuse (measured consumer
     // rates 64% vs 72% of the HBM rate at M = 16).
-    int cand[2], nc = 0;
+    int cand[3], nc = 0;
     if (a.M > 16) {
         cand[nc++] = 4;
     } else if (a.M > 8) {
         cand[nc++] = 2;
         cand[nc++] = 3;
+        cand[nc++] = 5;
     } else {
         cand[nc++] = 0;
         cand[nc++] = 1;
@@ -1150,9 +1161,12 @@ QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
         const int rows = qmv::kVariantRows[v];
         const int64_t nblocks = (a.N + rows - 1) / rows;
         const int64_t items = nblocks * spb;
+        // Variant 5 only as a data-parallel plan: every block whole in one CTA
+        // and nearly every SM busy, so no block is combined across CTAs.
+        if (v == 5 && (nblocks > num_sms || nblocks * 8 < num_sms * 7)) continue;
         // The fewest CTAs with the makespan of one per SM: fewer contributors
-        // per block, less partial traffic.
-        const int64_t per_sm = (items + num_sms - 1) / num_sms;
+        // per block, less partial traffic (variant 5: one block per CTA).
+        const int64_t per_sm = v == 5 ? spb : (items + num_sms - 1) / num_sms;
         const int grid = static_cast<int>((items + per_sm - 1) / per_sm);
         // Contributors per block: a block spans at most ceil(spb / floor(items/grid)) + 1 CTAs.
         const int64_t per_cta = std::max<int64_t>(1, items / grid);
@@ -1160,7 +1174,11 @@ QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
         const size_t need = kPartialOffset + static_cast<size_t>(nblocks) * max_slots * a.M * rows * 4 +
                             qmv_prep_bytes(a);
         if (need > workspace_bytes) continue;
-        const double cost = double(per_sm) * rows * (qmv::kVariantNT[v] == 1 ? 1.12 : 1.0);
+        // Plans that combine blocks across CTAs pay for the split-K tail
+        // (partial sums written, waited for and re-read: ~20% of a gate/up
+        // launch measured).
+        const bool shared = items % grid != 0 || (items / grid) % spb != 0;
+        const double cost = double(per_sm) * rows * (qmv::kVariantNT[v] == 1 ? 1.12 : 1.0) * (shared ? 1.2 : 1.0);
         if (best.splits && cost >= best_cost) continue;
         QmvPlan p{};
         p.splits = 1;
@@ -1267,7 +1285,7 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     const CUtensorMap *wm, *sm, *bm, *xm;
     const uint64_t words = static_cast<uint64_t>(a.K) * a.bits / 32;
     const uint32_t xr = a.M > 16 ? 32 : 16;
-    const uint32_t box_rows = plan.variant >= 2 ? 160 : 192;  // 16 rows per consumer warp
+    const uint32_t box_rows = qmv::kVariantBoxRows[plan.variant];  // 16 rows per consumer warp
     if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32,
                                     box_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
         !(sm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2, 8,
@@ -1285,6 +1303,8 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
                       : launch_cfg<8, 1, 1, 12>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
     case 2: return b4 ? launch_cfg<4, 2, 2, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
                       : launch_cfg<8, 2, 2, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
+    case 5: return b4 ? launch_cfg<4, 2, 1, 13>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                      : launch_cfg<8, 2, 1, 13>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
     case 3: return b4 ? launch_cfg<4, 2, 1, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
                       : launch_cfg<8, 2, 1, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl);
     default: return b4 ? launch_cfg<4, 4, 1, 10>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)

@@ -138,6 +138,25 @@ def test_split_k_is_deterministic(ctx):
     assert torch.equal(y1, y2)
 
 
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("M", [12, 16])
+def test_qmv_whole_k_blocks(ctx, M, bits):
+    """The gate/up shape (N = 28672) takes the data-parallel plan: 208-row
+    blocks, each streamed over the whole K by one CTA (no split-K combine).
+    Sampled rows (including the last, partial block) within 1e-5 of float64,
+    and the same bits twice."""
+    N, K = 28672, 4096
+    data = synthetic.quantized_linear(M, N, K, bits=bits, seed=21)
+    bufs = _upload(ctx, data)
+    y1, sel = _run_dense(ctx, data, bufs)
+    assert "over 138 CTAs" in sel.reason.decode(), sel.reason
+    y2, _ = _run_dense(ctx, data, bufs)
+    assert torch.equal(y1, y2)
+    rows = np.concatenate([np.linspace(0, N - 209, 500).astype(np.int64), np.arange(N - 208, N)])
+    ref = _oracle_rows_f64(data, rows)
+    assert np.abs(y1.cpu().numpy()[:, rows] - ref).max() <= 1e-5 * max(1, np.abs(ref).max())
+
+
 @pytest.mark.parametrize("M", [17, 33, 63, 64, 100])
 def test_qmv_multi_pass(ctx, M):
     """M > 32 below 64 runs qmv passes over 32-row slices; from 64 rows the
