@@ -178,9 +178,15 @@ int select_impl(const affon_b200_qmm_desc *d, const afb::QmmArgs &a, int num_sms
     if (qmv_plannable && a.M <= afb::kMaxQmvRows) {
         c.impl = IMPL_QMV;
         c.plan = qplan;
-        snprintf(reason, sizeof reason,
-                 "M=%lld <= 32: decode qmv, stream-K over %d CTAs, up to %d K segments per tile, %d-stage ring",
-                 (long long)a.M, c.plan.grid_n, c.plan.max_slots, c.plan.stages);
+        if (c.plan.variant >= 6)
+            snprintf(reason, sizeof reason,
+                     "M=%lld <= 32: decode qmv, %d-row whole-K blocks over %d CTAs, K split over the warps of a CTA, "
+                     "%d-stage ring",
+                     (long long)a.M, c.plan.rows, c.plan.grid_n, c.plan.stages);
+        else
+            snprintf(reason, sizeof reason,
+                     "M=%lld <= 32: decode qmv, stream-K over %d CTAs, up to %d K segments per tile, %d-stage ring",
+                     (long long)a.M, c.plan.grid_n, c.plan.max_slots, c.plan.stages);
     } else if (tc_ok && d->numerical_policy == AFFON_B200_POLICY_APPROXIMATE) {
         c.impl = IMPL_QMM_TC;
         snprintf(reason, sizeof reason, "M=%lld >= 64: tcgen05 qmm with bf16-rounded decoded weights", (long long)a.M);

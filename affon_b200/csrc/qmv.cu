@@ -75,6 +75,7 @@ namespace qmv {
 
 constexpr int GROUP = 64;
 constexpr int MAX_STAGES = 8;
+constexpr int MAX_WS_STAGES = 20;  // ring depth of the warp-split kernel, at most
 constexpr int MAX_XR = 32;             // activation rows staged per group, at most
 
 // Consumer warps (CW), 16-row weight tiles per consumer warp (NT) and 8-row
@@ -105,10 +106,11 @@ struct Shape {
 // -> 384, 1 = (1, 1, 12) -> 192; M <= 16: 2 = (2, 2, 10) -> 320, 3 = (2, 1, 10)
 // -> 160, 5 = (2, 1, 13) -> 208 (whole-K blocks, one per CTA); M <= 32: 4 =
 // (4, 1, 10) -> 160.  The planner picks, per shape, the variant with the
-// smallest estimated makespan.
-constexpr int kVariantRows[6] = {384, 192, 320, 160, 160, 208};
-constexpr int kVariantNT[6] = {2, 1, 2, 1, 1, 1};
-constexpr int kVariantBoxRows[6] = {192, 192, 160, 160, 160, 208};  // 16 rows per consumer warp
+// smallest estimated makespan.  Variants 6, 7, 8: the warp-split whole-K
+// kernel (qmv_ws_kernel) with T = 1, 2, 3 tiles -> 16, 32, 48 rows, M <= 16.
+constexpr int kVariantRows[9] = {384, 192, 320, 160, 160, 208, 16, 32, 48};
+constexpr int kVariantNT[9] = {2, 1, 2, 1, 1, 1, 1, 1, 1};
+constexpr int kVariantBoxRows[9] = {192, 192, 160, 160, 160, 208, 16, 32, 48};  // one box per block row tile set
 static_assert(Shape<4, 1, 2, 12>::BOX_ROWS == kVariantBoxRows[0] && Shape<4, 1, 1, 12>::BOX_ROWS == kVariantBoxRows[1] &&
                   Shape<4, 2, 2, 10>::BOX_ROWS == kVariantBoxRows[2] && Shape<4, 2, 1, 10>::BOX_ROWS == kVariantBoxRows[3] &&
                   Shape<4, 4, 1, 10>::BOX_ROWS == kVariantBoxRows[4] && Shape<4, 2, 1, 13>::BOX_ROWS == kVariantBoxRows[5],
@@ -180,15 +182,18 @@ __device__ __forceinline__ int pair_slot(int e) { return (e < 4) ? 2 * e : 2 * (
 // Residual update of one element: h += v, the next projection's
 // activation bf16(h * gamma_next) at its column-order position when asked,
 // and the square for the sums of squares.
+// h_pre / g_pre: h[m][n] and next_gamma[n] already loaded by the caller
+// (their loads issued together with the caller's other loads).
 __device__ __forceinline__ float resid_update(const Params &p, int m, int64_t n, float v, float &ssq,
-                                              const float *h_pre = nullptr) {
+                                              const float *h_pre = nullptr, const float *g_pre = nullptr) {
     float *h = p.f.h_out + m * p.f.ld_h_out;
     const float hv = (h_pre ? *h_pre : h[n]) + v;
     h[n] = hv;
     if (p.f.next_x) {
         const int e = static_cast<int>(n & 7);
         const int64_t col = p.f.next_pair_order ? (n & ~int64_t(7)) + pair_slot(e) : n;
-        p.f.next_x[m * p.f.ld_next_x + col] = f32_to_bf16_bits(hv * bf16_bits_to_f32(p.f.next_gamma[n]));
+        const float gm = g_pre ? *g_pre : bf16_bits_to_f32(p.f.next_gamma[n]);
+        p.f.next_x[m * p.f.ld_next_x + col] = f32_to_bf16_bits(hv * gm);
     }
     ssq = fmaf(hv, hv, ssq);
     return hv;
@@ -225,8 +230,11 @@ __device__ __forceinline__ void ar_signal(const Params &p, int unit, int tid) {
     }
 }
 
+// pre (EPI_RESID): h[m][n_lo], h[m][n_hi], next_gamma[n_lo], next_gamma[n_hi]
+// already loaded by the caller.
 __device__ __forceinline__ unsigned long long epilogue_pair(const Params &p, int m, int64_t n_lo, float v_lo,
-                                                            float v_hi, float &ssq, const float *rs) {
+                                                            float v_hi, float &ssq, const float *rs,
+                                                            const float *pre = nullptr) {
     const int64_t n_hi = n_lo + 8;
     const bool ok_lo = n_lo < p.N, ok_hi = n_hi < p.N;
     unsigned long long best = 0ull;
@@ -236,8 +244,9 @@ __device__ __forceinline__ unsigned long long epilogue_pair(const Params &p, int
     }
     switch (p.f.epi) {
     case EPI_RESID: {
-        if (ok_lo) resid_update(p, m, n_lo, v_lo, ssq);
-        if (ok_hi) resid_update(p, m, n_hi, v_hi, ssq);
+        const bool g = pre && p.f.next_x;
+        if (ok_lo) resid_update(p, m, n_lo, v_lo, ssq, pre ? &pre[0] : nullptr, g ? &pre[2] : nullptr);
+        if (ok_hi) resid_update(p, m, n_hi, v_hi, ssq, pre ? &pre[1] : nullptr, g ? &pre[3] : nullptr);
         break;
     }
     case EPI_RESID_AR:
@@ -299,6 +308,26 @@ __device__ __forceinline__ void publish_tile(const Params &p, int64_t tile, int 
 template <int MT>
 __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT][4], int64_t n0, int g, int t,
                                             const float *rs) {
+    // The residual epilogue reads h and the next norm's weights: issue all of
+    // this thread's loads before its first store (one round trip, not one per
+    // element).
+    float pre[MT][2][4];
+    const bool resid = p.f.epi == EPI_RESID;
+    if (resid) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int m = 2 * t + 8 * mt + h;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int64_t n = n0 + g + 8 * e;
+                    const bool ok = m < p.M && n < p.N;
+                    pre[mt][h][e] = ok ? p.f.h_out[m * p.f.ld_h_out + n] : 0.0f;
+                    pre[mt][h][2 + e] = ok && p.f.next_x ? bf16_bits_to_f32(p.f.next_gamma[n]) : 0.0f;
+                }
+            }
+    }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -306,7 +335,7 @@ __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT
             const int m = 2 * t + 8 * mt + h;
             float ssq = 0.0f;
             unsigned long long best = 0ull;
-            if (m < p.M) best = epilogue_pair(p, m, n0 + g, v[mt][h], v[mt][2 + h], ssq, rs);
+            if (m < p.M) best = epilogue_pair(p, m, n0 + g, v[mt][h], v[mt][2 + h], ssq, rs, resid ? pre[mt][h] : nullptr);
             publish_tile(p, n0 >> 4, m, g == 0, ssq, best);
         }
 }
@@ -317,9 +346,9 @@ __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT
 // Residual update of rows n (one per lane, 32 consecutive rows per warp,
 // the same m) with the per-16-row sums of squares.  Called by all 32 lanes.
 __device__ __forceinline__ void resid_row(const Params &p, int m, int64_t n, float v, int lane, bool ok,
-                                          const float *h_pre = nullptr) {
+                                          const float *h_pre = nullptr, const float *g_pre = nullptr) {
     float ssq = 0.0f;
-    if (ok) resid_update(p, m, n, v, ssq, h_pre);
+    if (ok) resid_update(p, m, n, v, ssq, h_pre, g_pre);
     ssq += __shfl_xor_sync(0xffffffffu, ssq, 1);
     ssq += __shfl_xor_sync(0xffffffffu, ssq, 2);
     ssq += __shfl_xor_sync(0xffffffffu, ssq, 4);
@@ -328,12 +357,13 @@ __device__ __forceinline__ void resid_row(const Params &p, int m, int64_t n, flo
 }
 
 __device__ __forceinline__ void finish_row(const Params &p, int m, int64_t n, float v, int lane, bool active,
-                                           const float *rs, const float *h_pre = nullptr) {
+                                           const float *rs, const float *h_pre = nullptr,
+                                           const float *g_pre = nullptr) {
     const bool ok = active && n < p.N;
     if (rs) v *= rs[m];
     switch (p.f.epi) {
     case EPI_RESID:
-        resid_row(p, m, n, v, lane, ok, h_pre);
+        resid_row(p, m, n, v, lane, ok, h_pre, g_pre);
         break;
     case EPI_RESID_AR:
         if (ok) ar_push(p, m, n, v);
@@ -452,9 +482,9 @@ __device__ __forceinline__ SharedBlock shared_block(const Params &p, int blk) {
 template <int ROWS, int CW>
 __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp, int lane, int tid,
                                volatile int *abort, const float *rs, uint64_t *rsbar) {
-    // Units per batch: eight where the 168-register variants have room, four
-    // in the 128-register ones.
-    constexpr int CT = CW * 32, UB = CW == 12 ? 4 : 8, MAXS = 4;
+    // Units per batch: three where the 168-register variants have room, two in
+    // the 128-register ones; slots per unit loaded together: MAXS.
+    constexpr int CT = CW * 32, UB = CW == 10 ? 3 : 2, MAXS = 16;
     if (hi <= lo) return;
     unsigned *done = p.counters + kMaxTiles / 2;
     const int b_first = static_cast<int>(lo / p.spb), b_last = static_cast<int>((hi - 1) / p.spb);
@@ -488,11 +518,14 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
     const float *baseA = p.partial + static_cast<int64_t>(A.blk) * p.max_slots * slot_stride;
     const float *baseB = p.partial + static_cast<int64_t>(B.blk) * p.max_slots * slot_stride;
     const int units = A.units + B.units;
+    const bool resid = p.f.epi == EPI_RESID, gamma = resid && p.f.next_x != nullptr;
     // Work unit = (block, 32-row chunk, activation row m), one warp each; a
-    // warp takes UB units at a time and issues every slot load of all of them
-    // before summing, so the combine costs about one L2 round trip per batch.
+    // warp takes UB units at a time and issues every load of all of them --
+    // up to MAXS slots each, and the residual row and next-norm weights the
+    // residual epilogue reads -- before summing, so a batch costs about one
+    // L2 round trip.
     for (int ub = warp; ub < units; ub += CW * UB) {
-        float part[UB][MAXS];
+        float part[UB][MAXS], hpre[UB], gpre[UB];
 #pragma unroll
         for (int u = 0; u < UB; ++u) {
             const int unit = ub + u * CW;
@@ -505,6 +538,10 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
             const float *src = (inB ? baseB : baseA) + static_cast<int64_t>(m) * ROWS + row;
 #pragma unroll
             for (int k = 0; k < MAXS; ++k) part[u][k] = (k < total && unit < units) ? __ldcg(src + k * slot_stride) : 0.0f;
+            const int64_t n = static_cast<int64_t>(inB ? B.blk : A.blk) * ROWS + row;
+            const bool ok = resid && unit < units && rr < nrows && n < p.N;
+            hpre[u] = ok ? p.f.h_out[m * p.f.ld_h_out + n] : 0.0f;
+            gpre[u] = ok && gamma ? bf16_bits_to_f32(p.f.next_gamma[n]) : 0.0f;
         }
         // Slots beyond MAXS (more than MAXS contributors) are added after.
 #pragma unroll
@@ -525,7 +562,8 @@ __device__ void combine_blocks(const Params &p, int64_t lo, int64_t hi, int warp
             for (int k = 0; k < MAXS; ++k)
                 if (k < total) v += part[u][k];
             for (int k = MAXS; k < total; ++k) v += __ldcg(src + k * slot_stride);
-            finish_row(p, m, static_cast<int64_t>(blk) * ROWS + row0 + rr, v, lane, active, rs);
+            finish_row(p, m, static_cast<int64_t>(blk) * ROWS + row0 + rr, v, lane, active, rs, resid ? &hpre[u] : nullptr,
+                       gamma ? &gpre[u] : nullptr);
         }
     }
     for (int k = 0; k < (two ? 2 : 1); ++k) {
@@ -578,7 +616,7 @@ __device__ void ar_finish(const Params &p, int64_t lo, int64_t hi, int warp, int
         const int units = ((nrows + 31) / 32) * p.M;
         constexpr int AUB = CW == 12 ? 2 : 4;  // units whose loads travel together
         for (int u0 = warp; u0 < units; u0 += CW * AUB) {
-            float part[AUB][kTpMaxWorld], hpre[AUB];
+            float part[AUB][kTpMaxWorld], hpre[AUB], gpre[AUB];
 #pragma unroll
             for (int k = 0; k < AUB; ++k) {
                 const int u = u0 + k * CW;
@@ -591,6 +629,7 @@ __device__ void ar_finish(const Params &p, int64_t lo, int64_t hi, int warp, int
                     part[k][r] = (ok && r < p.f.tp_world) ? __ldcg(recv + r * src_stride + static_cast<int64_t>(m) * p.N + n)
                                                          : 0.0f;
                 hpre[k] = ok ? p.f.h_out[m * p.f.ld_h_out + n] : 0.0f;
+                gpre[k] = ok && p.f.next_x ? bf16_bits_to_f32(p.f.next_gamma[n]) : 0.0f;
             }
 #pragma unroll
             for (int k = 0; k < AUB; ++k) {
@@ -604,7 +643,73 @@ __device__ void ar_finish(const Params &p, int64_t lo, int64_t hi, int warp, int
 #pragma unroll
                 for (int r = 0; r < kTpMaxWorld; ++r)
                     if (r < p.f.tp_world) v += part[k][r];
-                resid_row(p, m, n, v, lane, ok, &hpre[k]);
+                resid_row(p, m, n, v, lane, ok, &hpre[k], p.f.next_x ? &gpre[k] : nullptr);
+            }
+        }
+    }
+}
+
+// Group sums of one stage's activation columns: X_g[m] for the GPS groups
+// and every activation row, via m16n8k16 MMAs with an all-ones A operand
+// (rows equal, so lane (g, t) holds rows 2t, 2t+1 (+8 mt) in c[0], c[1]).
+// The shared loads of GB groups are issued before their first MMA and their
+// stores come last, so the MMA chains overlap instead of waiting on each
+// other's stores (GB = 0: one (group, row tile) at a time, for variants
+// without the registers).  Rows are written by the g == 0 lanes to
+// xs[G * XSTRIDE + m].
+template <int GPS, int MT, int X_BOX, int XSTRIDE, int GB>
+__device__ __forceinline__ void stage_group_sums(const char *xsb, float *xs, int g, int t) {
+    const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 1.0 pairs
+    if constexpr (GB == 0) {
+#pragma unroll
+        for (int G = 0; G < GPS; ++G)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const char *row = xsb + G * X_BOX + (g + 8 * mt) * 128;
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(row + (((2 * t) ^ g) << 4));
+                const uint4 v1 = *reinterpret_cast<const uint4 *>(row + (((2 * t + 1) ^ g) << 4));
+                float cx[4] = {0.f, 0.f, 0.f, 0.f};
+                mma_bf16_16816(cx, ones, v0.x, v0.y, cx);
+                mma_bf16_16816(cx, ones, v0.z, v0.w, cx);
+                mma_bf16_16816(cx, ones, v1.x, v1.y, cx);
+                mma_bf16_16816(cx, ones, v1.z, v1.w, cx);
+                if (g == 0) {
+                    xs[G * XSTRIDE + 8 * mt + 2 * t] = cx[0];
+                    xs[G * XSTRIDE + 8 * mt + 2 * t + 1] = cx[1];
+                }
+            }
+        return;
+    } else {
+#pragma unroll
+        for (int G0 = 0; G0 < GPS; G0 += GB) {
+            uint4 v[GB][MT][2];
+#pragma unroll
+            for (int G = 0; G < GB; ++G)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    const char *row = xsb + (G0 + G) * X_BOX + (g + 8 * mt) * 128;
+                    v[G][mt][0] = *reinterpret_cast<const uint4 *>(row + (((2 * t) ^ g) << 4));
+                    v[G][mt][1] = *reinterpret_cast<const uint4 *>(row + (((2 * t + 1) ^ g) << 4));
+                }
+            float cx[GB][MT][4];
+#pragma unroll
+            for (int G = 0; G < GB; ++G)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    cx[G][mt][0] = cx[G][mt][1] = cx[G][mt][2] = cx[G][mt][3] = 0.f;
+                    mma_bf16_16816(cx[G][mt], ones, v[G][mt][0].x, v[G][mt][0].y, cx[G][mt]);
+                    mma_bf16_16816(cx[G][mt], ones, v[G][mt][0].z, v[G][mt][0].w, cx[G][mt]);
+                    mma_bf16_16816(cx[G][mt], ones, v[G][mt][1].x, v[G][mt][1].y, cx[G][mt]);
+                    mma_bf16_16816(cx[G][mt], ones, v[G][mt][1].z, v[G][mt][1].w, cx[G][mt]);
+                }
+            if (g == 0) {
+#pragma unroll
+                for (int G = 0; G < GB; ++G)
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        xs[(G0 + G) * XSTRIDE + 8 * mt + 2 * t] = cx[G][mt][0];
+                        xs[(G0 + G) * XSTRIDE + 8 * mt + 2 * t + 1] = cx[G][mt][1];
+                    }
             }
         }
     }
@@ -707,84 +812,78 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
         pdl_wait();
         // Row scales rsqrt(sum_k h^2 / K + eps) of the unnormalised
         // activations from their per-16-column sums of squares: lane l adds
-        // tiles l, l + 32, ... for every row (two tiles' loads in flight at a
-        // time), then a butterfly per row -- the RMSNorm prologue's order.
-        // Only the epilogues use them, so they are formed once the first ring
-        // fill's group sums are out, while the consumers work on those stages,
-        // and published through s_rsbar.
-        auto row_scales = [&]() {
-            constexpr int RMAX = 8 * MT;  // activation rows this instantiation serves
-            float acc[RMAX];
+        // tiles l, l + 32, ... for every row, then a butterfly per row -- the
+        // RMSNorm prologue's order.  Only the epilogues use them, so their
+        // loads ride along the stage loop: each stage issues the next two
+        // tiles per lane before waiting for its data and adds them after its
+        // group sums, and the scales are published through s_rsbar.
+        constexpr int RMAX = 8 * MT, RQ = RMAX / 4;  // activation rows this instantiation serves
+        const int quads = (p.M + 3) / 4;
+        float racc[RMAX];
 #pragma unroll
-            for (int m = 0; m < RMAX; ++m) acc[m] = 0.0f;
-            const int quads = (p.M + 3) / 4;
-            for (int tl0 = lane; tl0 < p.f.ss_tiles; tl0 += 64) {
-                float4 v[2][RMAX / 4];
+        for (int m = 0; m < RMAX; ++m) racc[m] = 0.0f;
+        float4 rv[2][RQ];
+        int rs_left = p.f.row_ss ? max(1, (p.f.ss_tiles + 63) / 64) : 0, rtile = lane;
+        auto rs_issue = [&]() {
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int tl = tl0 + 32 * j;
-                    const float4 *row = reinterpret_cast<const float4 *>(p.f.row_ss + tl * kSsWidth);
+            for (int j = 0; j < 2; ++j) {
+                const int tl = rtile + 32 * j;
+                const float4 *row = reinterpret_cast<const float4 *>(p.f.row_ss + tl * kSsWidth);
 #pragma unroll
-                    for (int q = 0; q < RMAX / 4; ++q)
-                        v[j][q] = (tl < p.f.ss_tiles && q < quads) ? __ldcg(row + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int j = 0; j < 2; ++j)
-#pragma unroll
-                    for (int q = 0; q < RMAX / 4; ++q) {
-                        acc[4 * q] += v[j][q].x;
-                        acc[4 * q + 1] += v[j][q].y;
-                        acc[4 * q + 2] += v[j][q].z;
-                        acc[4 * q + 3] += v[j][q].w;
-                    }
+                for (int q = 0; q < RQ; ++q)
+                    rv[j][q] = (tl < p.f.ss_tiles && q < quads) ? __ldcg(row + q) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-#pragma unroll
-            for (int m = 0; m < RMAX; ++m) {
-                float sum = acc[m];
-#pragma unroll
-                for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                if (lane == 0 && m < p.M) s_rscale[m] = rsqrtf(sum / static_cast<float>(p.K) + p.f.eps);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_rsbar);
         };
-        const int64_t first_fill = lo + S < hi ? lo + S : hi;
+        auto rs_accum = [&]() {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int q = 0; q < RQ; ++q) {
+                    racc[4 * q] += rv[j][q].x;
+                    racc[4 * q + 1] += rv[j][q].y;
+                    racc[4 * q + 2] += rv[j][q].z;
+                    racc[4 * q + 3] += rv[j][q].w;
+                }
+            rtile += 64;
+            if (--rs_left == 0) {
+                // Butterfly of every row (levels outermost, so the rows'
+                // shuffle chains overlap), then lane m forms row m's scale.
+#pragma unroll
+                for (int o = 16; o; o >>= 1)
+#pragma unroll
+                    for (int m = 0; m < RMAX; ++m) racc[m] += __shfl_xor_sync(0xffffffffu, racc[m], o);
+                float mine = 0.0f;
+#pragma unroll
+                for (int m = 0; m < RMAX; ++m) mine = lane == m ? racc[m] : mine;
+                if (lane < RMAX && lane < p.M) s_rscale[lane] = rsqrtf(mine / static_cast<float>(p.K) + p.f.eps);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_rsbar);
+            }
+        };
         // X_g = sum_{k in g} x[m][k] for every activation row, once per CTA and
-        // stage, via m16n8k16 MMAs with an all-ones A operand (rows equal).
-        const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 1.0 pairs
+        // stage (stage_group_sums).
         int stage = 0;
         uint32_t phase = 0;
         for (int64_t i = lo; i < hi; ++i) {
-            if (p.f.row_ss && i == first_fill) row_scales();
+            const bool rs_step = rs_left > 0;
+            if (rs_step) rs_issue();
             mbar_wait(&full[stage], phase, abort, p.status);
             const char *xsb = ring + stage * Sh::BYTES + Sh::W + 2 * Sh::SB;
-            float *xs = xsums + stage * GPS * MAX_XR;
-#pragma unroll
-            for (int G = 0; G < GPS; ++G)
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    const char *row = xsb + G * Sh::X_BOX + (g + 8 * mt) * 128;
-                    const uint4 v0 = *reinterpret_cast<const uint4 *>(row + (((2 * t) ^ g) << 4));
-                    const uint4 v1 = *reinterpret_cast<const uint4 *>(row + (((2 * t + 1) ^ g) << 4));
-                    float cx[4] = {0.f, 0.f, 0.f, 0.f};
-                    mma_bf16_16816(cx, ones, v0.x, v0.y, cx);
-                    mma_bf16_16816(cx, ones, v0.z, v0.w, cx);
-                    mma_bf16_16816(cx, ones, v1.x, v1.y, cx);
-                    mma_bf16_16816(cx, ones, v1.z, v1.w, cx);
-                    if (g == 0) {  // cx[0], cx[1] = X of activation rows 2t, 2t+1 (+8 mt)
-                        xs[G * MAX_XR + 8 * mt + 2 * t] = cx[0];
-                        xs[G * MAX_XR + 8 * mt + 2 * t + 1] = cx[1];
-                    }
-                }
+            stage_group_sums<GPS, MT, Sh::X_BOX, MAX_XR, (MT > 2 ? 0 : CW >= 12 ? 1 : GPS)>(
+                xsb, xsums + stage * GPS * MAX_XR, g, t);
             fence_proxy_async_smem();  // x reads before the stage's next TMA fill
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&xsfull[stage]);
                 mbar_arrive(&empty[stage]);
             }
+            if (rs_step) rs_accum();
             if (++stage == S) { stage = 0; phase ^= 1; }
         }
-        if (p.f.row_ss && first_fill == hi) row_scales();  // a range no longer than the ring
+        while (rs_left > 0) {  // a range shorter than the tiles' loads
+            rs_issue();
+            rs_accum();
+        }
     } else {  // ------------------------------------------------- consumers
         pdl_wait();
         int stage = 0;
@@ -941,6 +1040,340 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
         }
         combine_blocks<ROWS, CW>(p, lo, hi, warp, lane, tid, abort, rs, &s_rsbar);
         if (p.f.epi == EPI_RESID_AR) ar_finish<ROWS, CW>(p, lo, hi, warp, lane, tid, abort);
+    }
+}
+
+// Warp-split whole-K kernel (M <= 16, N up to three 16-row tiles per SM).
+// One block of T 16-row tiles per CTA, streamed over the whole K range once,
+// so no block is combined across CTAs: consumer warp (tile t, K lane k of
+// KW) takes stages k, k + KW, k + 2 KW, ... of tile t.  One sum warp forms
+// the group sums X_g of every stage, as in the stream-K kernel (same MMAs,
+// same order), into a small shared ring beside the stage ring, so the affine
+// per-group step is the stream-K kernel's.  The K lanes' accumulators meet in
+// shared memory and are added in lane order (results do not depend on
+// scheduling); the lane-0 warps apply the epilogue.  The ring depth is a
+// multiple of KW, so every ring slot serves the stages of one K lane only: a
+// warp waiting on a slot has consumed the slot's previous stage itself, and
+// its parity wait never runs a phase ahead.  A stage is two TMA loads (the
+// packed rows; the activation columns of its groups as one 3D box), the
+// block's scales and biases one load each per launch: at these block heights
+// the TMA work per stage, not its bytes, sets the streaming rate.  The
+// producer warp forms the RMSNorm row scales after its first ring fill.
+template <int BITS, int MT, int T>
+struct WsShape {
+    static constexpr int KW = T == 3 ? 3 : 10 / T;  // K lanes
+    static constexpr int CW = T * KW;               // consumer warps
+    static constexpr int THREADS = 32 * (CW + 2);   // consumers, producer, sum warp
+    static constexpr int ROWS = 16 * T;
+    static constexpr int XR = 16;
+    static constexpr int X_BOX = XR * 128;
+    static constexpr int GPS = BITS == 4 ? 4 : 2;
+    static constexpr int KPS = GPS * GROUP;
+    static constexpr int W = ROWS * 128;
+    static constexpr int X = GPS * X_BOX;
+    static constexpr int BYTES = W + X;     // a ring stage: packed rows, then the activation columns
+    static constexpr int TX_BYTES = W + X;  // bytes the stage's two TMA loads deliver
+    static constexpr int RED = KW * T * MT * 4 * 32 * 4;  // the K lanes' accumulators
+    static_assert(W % 1024 == 0 && X % 1024 == 0 && RED % 16 == 0, "stage layout");
+};
+
+// Scales and biases of a warp-split block live in shared memory for the
+// whole launch (one load each): [ROWS][pitch] bf16, the pitch the group count
+// rounded up to 16 plus 8, so the eight rows a warp reads at once fall in
+// distinct banks (pitch/2 words = 4 mod 8).  The padding columns are read
+// beyond the tensor's extent and come back zero.
+__host__ __device__ constexpr int ws_slab_pitch(int K) { return (K / GROUP + 15) / 16 * 16 + 8; }
+__host__ __device__ constexpr int ws_slab_bytes(int rows, int K) { return (2 * rows * ws_slab_pitch(K) * 2 + 127) / 128 * 128; }
+
+static_assert(WsShape<4, 2, 1>::ROWS == kVariantBoxRows[6] && WsShape<4, 2, 2>::ROWS == kVariantBoxRows[7] &&
+                  WsShape<4, 2, 3>::ROWS == kVariantBoxRows[8],
+              "tensor-map boxes match the warp-split kernels' blocks");
+
+// Row scales of the RMSNorm prologue, one warp: lane l adds tiles l, l + 32,
+// ... (four tiles' loads in flight per round), then a butterfly per row --
+// the same order as the stream-K kernel and the prep kernel.
+template <int MT>
+__device__ void ws_row_scales(const Params &p, int lane, float *s_rscale, uint64_t *bar) {
+    constexpr int RMAX = 8 * MT, RQ = RMAX / 4, TPR = 4;
+    const int quads = (p.M + 3) / 4;
+    float racc[RMAX];
+#pragma unroll
+    for (int m = 0; m < RMAX; ++m) racc[m] = 0.0f;
+    for (int tl0 = lane; tl0 < p.f.ss_tiles; tl0 += 32 * TPR) {
+        float4 v[TPR][RQ];
+#pragma unroll
+        for (int j = 0; j < TPR; ++j) {
+            const int tl = tl0 + 32 * j;
+            const float4 *row = reinterpret_cast<const float4 *>(p.f.row_ss + tl * kSsWidth);
+#pragma unroll
+            for (int q = 0; q < RQ; ++q)
+                v[j][q] = (tl < p.f.ss_tiles && q < quads) ? __ldcg(row + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < TPR; ++j)
+#pragma unroll
+            for (int q = 0; q < RQ; ++q) {
+                racc[4 * q] += v[j][q].x;
+                racc[4 * q + 1] += v[j][q].y;
+                racc[4 * q + 2] += v[j][q].z;
+                racc[4 * q + 3] += v[j][q].w;
+            }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+        for (int m = 0; m < RMAX; ++m) racc[m] += __shfl_xor_sync(0xffffffffu, racc[m], o);
+    float mine = 0.0f;
+#pragma unroll
+    for (int m = 0; m < RMAX; ++m) mine = lane == m ? racc[m] : mine;
+    if (lane < RMAX && lane < p.M) s_rscale[lane] = rsqrtf(mine / static_cast<float>(p.K) + p.f.eps);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+}
+
+template <int BITS, int MT, int T>
+__global__ void __launch_bounds__(WsShape<BITS, MT, T>::THREADS, 1)
+    qmv_ws_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                  const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap xmap, Params p) {
+    using Sh = WsShape<BITS, MT, T>;
+    constexpr int GPS = Sh::GPS, KPS = Sh::KPS, KW = Sh::KW, CW = Sh::CW, ROWS = Sh::ROWS;
+    extern __shared__ char smem_raw[];
+    char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = p.stages;  // a multiple of KW
+    const int SP = ws_slab_pitch(p.K);
+    char *ring = smem;
+    char *slab = ring + S * Sh::BYTES;  // scales [ROWS][SP], then biases [ROWS][SP]
+    float *red = reinterpret_cast<float *>(slab + ws_slab_bytes(ROWS, p.K));
+    float *xsums = red + Sh::RED / 4;  // [slot][group][16 activation rows]
+    uint64_t *full = reinterpret_cast<uint64_t *>(xsums + MAX_WS_STAGES * GPS * 16);
+    uint64_t *empty = full + MAX_WS_STAGES;
+    uint64_t *xsfull = empty + MAX_WS_STAGES;
+    uint64_t *sbfull = xsfull + MAX_WS_STAGES;
+    volatile int *abort = reinterpret_cast<volatile int *>(sbfull + 1);
+    __shared__ float s_rscale[MAX_XR];  // RMSNorm row scales (row_scale mode)
+    __shared__ uint64_t s_rsbar;        // completes once s_rscale holds them
+    const float *rs = p.f.row_ss ? s_rscale : nullptr;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_launch_dependents();
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], T + 1);  // the T warps of the slot's K lane and the sum warp
+            mbar_init(&xsfull[s], 1);
+        }
+        mbar_init(sbfull, 1);
+        mbar_init(&s_rsbar, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const int blk = blockIdx.x, spb = p.spb;
+    const int g = lane >> 2, t = lane & 3;
+
+    if (warp == CW) {  // ------------------------------------------ producer
+        const uint64_t stream_policy = l2_evict_first();
+        const int row0 = blk * ROWS, pre = min(spb, S);
+        auto load_params = [&](int slot, int j) {
+            mbar_arrive_expect_tx(&full[slot], Sh::TX_BYTES);
+            tma_load_2d_hint(ring + slot * Sh::BYTES, &wmap, &full[slot], j * KPS * BITS / 32, row0, stream_policy);
+        };
+        auto load_x = [&](int slot, int j) {  // box: 64 columns x 16 rows x GPS groups
+            tma_load_3d(ring + slot * Sh::BYTES + Sh::W, &xmap, &full[slot], 0, 0, j * GPS);
+        };
+        if (lane == 0) {
+            tma_prefetch_desc(&wmap);
+            tma_prefetch_desc(&smap);
+            tma_prefetch_desc(&bmap);
+            tma_prefetch_desc(&xmap);
+            // The block's scales and biases (box: SP groups x ROWS rows).
+            mbar_arrive_expect_tx(sbfull, 2 * ROWS * SP * 2);
+            tma_load_2d_hint(slab, &smap, sbfull, 0, row0, stream_policy);
+            tma_load_2d_hint(slab + ROWS * SP * 2, &bmap, sbfull, 0, row0, stream_policy);
+            // Weights of the first ring fill need nothing from the preceding
+            // kernel; the activations do.
+            for (int j = 0; j < pre; ++j) load_params(j, j);
+            pdl_wait();
+            for (int j = 0; j < pre; ++j) load_x(j, j);
+        }
+        // The row scales (all lanes), while the first ring fill lands and is
+        // consumed: no refill is due before the first stage is released.
+        __syncwarp();
+        if (rs) {
+            pdl_wait();
+            ws_row_scales<MT>(p, lane, s_rscale, &s_rsbar);
+        }
+        if (lane == 0) {
+            uint32_t issued_mask = pre >= 32 ? ~0u : (1u << pre) - 1u, issued_par = 0;
+            for (int j = pre; j < spb; ++j) {
+                const int slot = j % S;
+                const uint32_t ph = static_cast<uint32_t>(j / S) & 1u;
+                // Never re-arm a slot after an abort (see the stream-K producer).
+                if (!mbar_wait(&empty[slot], ph ^ 1u, abort, p.status) || *abort) break;
+                load_params(slot, j);
+                load_x(slot, j);
+                issued_mask |= 1u << slot;
+                issued_par = (issued_par & ~(1u << slot)) | (ph << slot);
+            }
+            for (int s = 0; s < S; ++s)
+                if (issued_mask & (1u << s)) mbar_wait_drain(&full[s], (issued_par >> s) & 1u);
+            mbar_wait_drain(sbfull, 0);
+        }
+        __syncwarp();
+    } else if (warp == CW + 1) {  // ----------------------------- group sums
+        // X_g = sum_{k in g} x[m][k] for every activation row and stage
+        // (stage_group_sums).
+        for (int j = 0; j < spb; ++j) {
+            const int slot = j % S;
+            const uint32_t ph = static_cast<uint32_t>(j / S) & 1u;
+            mbar_wait(&full[slot], ph, abort, p.status);
+            stage_group_sums<GPS, MT, Sh::X_BOX, 16, GPS>(ring + slot * Sh::BYTES + Sh::W, xsums + slot * GPS * 16, g,
+                                                          t);
+            fence_proxy_async_smem();  // x reads before the slot's next TMA fill
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&xsfull[slot]);
+                mbar_arrive(&empty[slot]);
+            }
+        }
+    } else {  // ------------------------------------------------- consumers
+        pdl_wait();
+        const int tile = warp % T, kl = warp / T;
+        uint64_t acc[MT][2];  // packed f32 pairs: [..][0] = (c0, c1), [..][1] = (c2, c3)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = 0ull;
+        if (kl < spb) mbar_wait(sbfull, 0, abort, p.status);
+        const char *ssl = slab + (tile * 16 + g) * SP * 2, *bsl = ssl + ROWS * SP * 2;  // row r; row r + 8 at +8 SP
+        for (int j = kl; j < spb; j += KW) {
+            const int slot = j % S;
+            const uint32_t ph = static_cast<uint32_t>(j / S) & 1u;
+            mbar_wait(&full[slot], ph, abort, p.status);
+            const char *sw = ring + slot * Sh::BYTES;
+            const char *xsb = sw + Sh::W;
+            const float *xs = xsums + slot * GPS * 16;
+            uint32_t sv[2][GPS / 2], bv[2][GPS / 2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int off = h * 8 * SP * 2 + j * GPS * 2;  // groups j*GPS .. j*GPS+GPS-1
+                if constexpr (GPS == 4) {
+                    const uint2 a2 = *reinterpret_cast<const uint2 *>(ssl + off);
+                    const uint2 b2 = *reinterpret_cast<const uint2 *>(bsl + off);
+                    sv[h][0] = a2.x; sv[h][1] = a2.y; bv[h][0] = b2.x; bv[h][1] = b2.y;
+                } else {
+                    sv[h][0] = *reinterpret_cast<const uint32_t *>(ssl + off);
+                    bv[h][0] = *reinterpret_cast<const uint32_t *>(bsl + off);
+                }
+            }
+            mbar_wait(&xsfull[slot], ph, abort, p.status);
+#pragma unroll
+            for (int G = 0; G < GPS; ++G) {
+                uint32_t xf[MT][8];
+                const char *xb = xsb + G * Sh::X_BOX;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    const char *row = xb + (g + 8 * mt) * 128;
+                    const uint4 v0 = *reinterpret_cast<const uint4 *>(row + (((2 * t) ^ g) << 4));
+                    const uint4 v1 = *reinterpret_cast<const uint4 *>(row + (((2 * t + 1) ^ g) << 4));
+                    xf[mt][0] = v0.x; xf[mt][1] = v0.y; xf[mt][2] = v0.z; xf[mt][3] = v0.w;
+                    xf[mt][4] = v1.x; xf[mt][5] = v1.y; xf[mt][6] = v1.z; xf[mt][7] = v1.w;
+                }
+                uint32_t a[4][4];
+                const char *tw = sw + (tile * 16 + g) * 128;  // rows r and r + 8
+                if constexpr (BITS == 4) {
+                    const int off = (((2 * G + (t >> 1)) ^ g) << 4) + (t & 1) * 8;
+                    const uint2 u0 = *reinterpret_cast<const uint2 *>(tw + off);
+                    const uint2 u1 = *reinterpret_cast<const uint2 *>(tw + 8 * 128 + off);
+                    const uint32_t w0[2] = {u0.x, u0.y}, w1[2] = {u1.x, u1.y};
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        const int p0 = 2 * (s & 1);
+                        a[s][0] = dec4(w0[s >> 1], p0);
+                        a[s][1] = dec4(w1[s >> 1], p0);
+                        a[s][2] = dec4(w0[s >> 1], p0 + 1);
+                        a[s][3] = dec4(w1[s >> 1], p0 + 1);
+                    }
+                } else {
+                    const int off = ((4 * G + t) ^ g) << 4;
+                    const uint4 u0 = *reinterpret_cast<const uint4 *>(tw + off);
+                    const uint4 u1 = *reinterpret_cast<const uint4 *>(tw + 8 * 128 + off);
+                    const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w}, w1[4] = {u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        a[s][0] = dec8(w0[s], 0);
+                        a[s][1] = dec8(w1[s], 0);
+                        a[s][2] = dec8(w0[s], 2);
+                        a[s][3] = dec8(w1[s], 2);
+                    }
+                }
+                float c[MT][4];
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) c[mt][i] = 0.f;
+#pragma unroll
+                for (int s = 0; s < 4; ++s)
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        const uint32_t b0 = BITS == 4 ? xf[mt][4 * (s >> 1) + 2 * (s & 1)] : xf[mt][2 * s];
+                        const uint32_t b1 = BITS == 4 ? xf[mt][4 * (s >> 1) + 2 * (s & 1) + 1] : xf[mt][2 * s + 1];
+                        mma_bf16_16816(c[mt], a[s], b0, b1, c[mt]);
+                    }
+                const uint32_t s_w0 = sv[0][G >> 1], s_w1 = sv[1][G >> 1];
+                const uint32_t b_w0 = bv[0][G >> 1], b_w1 = bv[1][G >> 1];
+                const float s0 = __uint_as_float((G & 1) ? (s_w0 & 0xFFFF0000u) : (s_w0 << 16));
+                const float s1 = __uint_as_float((G & 1) ? (s_w1 & 0xFFFF0000u) : (s_w1 << 16));
+                float q0 = __uint_as_float((G & 1) ? (b_w0 & 0xFFFF0000u) : (b_w0 << 16));
+                float q1 = __uint_as_float((G & 1) ? (b_w1 & 0xFFFF0000u) : (b_w1 << 16));
+                if constexpr (BITS == 4) {  // codes entered the MMA as 128+q
+                    q0 = fmaf(-128.0f, s0, q0);
+                    q1 = fmaf(-128.0f, s1, q1);
+                }
+                const uint64_t s0p = f2_pack(s0, s0), s1p = f2_pack(s1, s1);
+                const uint64_t q0p = f2_pack(q0, q0), q1p = f2_pack(q1, q1);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    const uint64_t xsum = *reinterpret_cast<const uint64_t *>(xs + G * 16 + 8 * mt + 2 * t);
+                    acc[mt][0] = fma_f32x2(s0p, f2_pack(c[mt][0], c[mt][1]), fma_f32x2(q0p, xsum, acc[mt][0]));
+                    acc[mt][1] = fma_f32x2(s1p, f2_pack(c[mt][2], c[mt][3]), fma_f32x2(q1p, xsum, acc[mt][1]));
+                }
+            }
+            // The slot is refilled by TMA (async proxy) after this release;
+            // order this warp's generic-proxy reads of it first.
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        float accf[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            accf[mt][0] = __uint_as_float(static_cast<uint32_t>(acc[mt][0]));
+            accf[mt][1] = __uint_as_float(static_cast<uint32_t>(acc[mt][0] >> 32));
+            accf[mt][2] = __uint_as_float(static_cast<uint32_t>(acc[mt][1]));
+            accf[mt][3] = __uint_as_float(static_cast<uint32_t>(acc[mt][1] >> 32));
+        }
+        // K lanes 1..KW-1 hand their sums to lane 0 of their tile, which adds
+        // them in lane order.  red[((k * T + tile) * MT + mt) * 4 + i][lane].
+        if (kl > 0) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) red[(((kl * T + tile) * MT + mt) * 4 + i) * 32 + lane] = accf[mt][i];
+        }
+        named_bar_sync(1, CW * 32);
+        if (kl == 0) {
+            for (int k = 1; k < KW; ++k)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) accf[mt][i] += red[(((k * T + tile) * MT + mt) * 4 + i) * 32 + lane];
+            if (rs) mbar_wait(&s_rsbar, 0, abort, p.status);  // the row scales are out
+            finish_tile<MT>(p, accf, static_cast<int64_t>(blk) * ROWS + tile * 16, g, t, rs);
+        }
+        if (p.f.epi == EPI_RESID_AR) {
+            ar_signal<CW>(p, blk * p.max_slots, tid);
+            ar_finish<ROWS, CW>(p, static_cast<int64_t>(blk) * spb, static_cast<int64_t>(blk + 1) * spb, warp, lane,
+                                tid, abort);
+        }
     }
 }
 
@@ -1133,7 +1566,56 @@ int stage_bytes(int bits, int variant) {
 
 }  // namespace
 
+// Warp-split whole-K plan (qmv_ws_kernel): M <= 16, at most three 16-row
+// tiles per SM and at most 32 stages of K; one block of T tiles per CTA, no
+// combine across CTAs.  Each CTA streams the whole activation matrix beside
+// its 16-48 weight rows, so beyond 32 stages (K 8192 at 4 bits) the stream-K
+// plan, whose blocks amortise the activations over 160-320 rows, is faster
+// (measured on the 8B down projection, K = 14336: 27 vs 33 us).
+static QmvPlan ws_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
+    QmvPlan p{};
+    if (a.M > 16 || a.K / (a.bits == 4 ? 256 : 128) > 32) return p;
+    const int64_t tiles = (a.N + 15) / 16;
+    const int T = static_cast<int>((tiles + num_sms - 1) / num_sms);
+    if (T > 3) return p;
+    const bool mt2 = a.M > 8, b4 = a.bits == 4;
+    int bytes, red, kw;
+    switch (T) {
+    case 1: bytes = qmv::WsShape<4, 2, 1>::BYTES; kw = qmv::WsShape<4, 2, 1>::KW; red = qmv::WsShape<4, 2, 1>::RED; break;
+    case 2: bytes = qmv::WsShape<4, 2, 2>::BYTES; kw = qmv::WsShape<4, 2, 2>::KW; red = qmv::WsShape<4, 2, 2>::RED; break;
+    default: bytes = qmv::WsShape<4, 2, 3>::BYTES; kw = qmv::WsShape<4, 2, 3>::KW; red = qmv::WsShape<4, 2, 3>::RED; break;
+    }
+    (void)b4;  // the stage layout does not depend on the code width (128 packed bytes per row)
+    if (!mt2) red /= 2;
+    const int rows = 16 * T;
+    if (qmv::ws_slab_pitch(static_cast<int>(a.K)) > 256) return p;  // one TMA box per slab
+    // alignment slack, scale/bias slabs, K-lane sums, group-sum ring
+    // (4 groups x 16 rows per slot at most), full/empty/xsfull barriers and
+    // the slab barrier, the abort word
+    const int overhead = 1024 + qmv::ws_slab_bytes(rows, static_cast<int>(a.K)) + red +
+                         qmv::MAX_WS_STAGES * 4 * 16 * 4 + (3 * qmv::MAX_WS_STAGES + 1) * 8 + 64;
+    int stages = std::min(qmv::MAX_WS_STAGES, (kSmemCap - overhead) / bytes);
+    stages -= stages % kw;  // every ring slot serves one K lane
+    if (stages < kw) return p;
+    const int64_t nblocks = (a.N + rows - 1) / rows;
+    const size_t need = kPartialOffset + static_cast<size_t>(nblocks) * a.M * rows * 4 + qmv_prep_bytes(a);
+    if (need > workspace_bytes) return p;
+    p.splits = 1;
+    p.ks = static_cast<int>(a.K);
+    p.grid_n = static_cast<int>(nblocks);
+    p.stages = stages;
+    p.max_slots = 1;
+    p.smem_bytes = overhead + stages * bytes;
+    p.variant = 5 + T;
+    p.rows = rows;
+    return p;
+}
+
 QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
+    {
+        const QmvPlan w = ws_plan(a, num_sms, workspace_bytes);
+        if (w.splits) return w;
+    }
     // Candidates for this M; each is scored by its makespan in weight
     // row-stages (items per CTA x block rows), with one-tile-per-warp variants
     // charged 12% for their lower activation-fragment reuse (measured consumer
@@ -1234,6 +1716,21 @@ static cudaError_t launch_cfg(const CUtensorMap &wm, const CUtensorMap &sm, cons
     return e;
 }
 
+template <int BITS, int MT, int T>
+static cudaError_t launch_ws(const CUtensorMap &wm, const CUtensorMap &sm, const CUtensorMap &bm,
+                             const CUtensorMap &xm, const qmv::Params &p, const QmvPlan &plan, cudaStream_t stream,
+                             bool pdl) {
+    auto kern = qmv::qmv_ws_kernel<BITS, MT, T>;
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(kern), plan.smem_bytes);
+    if (e != cudaSuccess) return e;
+    // At most one CTA per SM and a grid no larger than the SM count: every
+    // CTA is resident (the fused exchange waits on peers' CTAs only).
+    e = launch_ex(kern, dim3(plan.grid_n), dim3(qmv::WsShape<BITS, MT, T>::THREADS), plan.smem_bytes, stream, !pdl,
+                  pdl, wm, sm, bm, xm, p);
+    count_launch();
+    return e;
+}
+
 cudaError_t launch_qmv_prep(const void *src, int64_t ld_src, int mode, const float *ss, int ss_tiles,
                             const uint16_t *gamma, float eps, int M, int K, int bits, uint16_t *dst, int64_t ld_dst,
                             cudaStream_t stream, bool pdl) {
@@ -1284,6 +1781,34 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
     }
     const CUtensorMap *wm, *sm, *bm, *xm;
     const uint64_t words = static_cast<uint64_t>(a.K) * a.bits / 32;
+    if (plan.variant >= 6) {  // warp-split: per-stage packed rows, 3D activation box, per-launch slabs
+        const uint32_t rows = static_cast<uint32_t>(plan.rows), sp = qmv::ws_slab_pitch(static_cast<int>(a.K));
+        const uint32_t gps = a.bits == 4 ? 4 : 2;
+        if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32,
+                                        rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+            !(sm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.s.ptr, a.K / 64, a.N, a.s.row_stride * 2,
+                                        sp, rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+            !(bm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2,
+                                        sp, rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+            !(xm = cached_tensor_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xq, 64, a.M, a.K / 64, ldxq * 2, 128, 64, 16,
+                                        gps, CU_TENSOR_MAP_SWIZZLE_128B)))
+            return cudaErrorInvalidValue;
+        const bool b4 = a.bits == 4, mt2 = a.M > 8;
+        switch (plan.variant) {
+        case 6: return b4 ? (mt2 ? launch_ws<4, 2, 1>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                                 : launch_ws<4, 1, 1>(*wm, *sm, *bm, *xm, p, plan, stream, pdl))
+                          : (mt2 ? launch_ws<8, 2, 1>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                                 : launch_ws<8, 1, 1>(*wm, *sm, *bm, *xm, p, plan, stream, pdl));
+        case 7: return b4 ? (mt2 ? launch_ws<4, 2, 2>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                                 : launch_ws<4, 1, 2>(*wm, *sm, *bm, *xm, p, plan, stream, pdl))
+                          : (mt2 ? launch_ws<8, 2, 2>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                                 : launch_ws<8, 1, 2>(*wm, *sm, *bm, *xm, p, plan, stream, pdl));
+        default: return b4 ? (mt2 ? launch_ws<4, 2, 3>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                                  : launch_ws<4, 1, 3>(*wm, *sm, *bm, *xm, p, plan, stream, pdl))
+                           : (mt2 ? launch_ws<8, 2, 3>(*wm, *sm, *bm, *xm, p, plan, stream, pdl)
+                                  : launch_ws<8, 1, 3>(*wm, *sm, *bm, *xm, p, plan, stream, pdl));
+        }
+    }
     const uint32_t xr = a.M > 16 ? 32 : 16;
     const uint32_t box_rows = qmv::kVariantBoxRows[plan.variant];  // 16 rows per consumer warp
     if (!(wm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w.ptr, words, a.N, a.w.row_stride * 4, 32,

@@ -94,6 +94,13 @@ AFB_DEVICE void tma_load_2d(void *smem_dst, const CUtensorMap *map, uint64_t *ba
         ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
 }
+// 3D tiled TMA load (coordinates innermost first).
+AFB_DEVICE void tma_load_3d(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
 // The same load with an L2 cache policy (e.g. l2_evict_first()).
 AFB_DEVICE void tma_load_2d_hint(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1,
                                  uint64_t policy) {
@@ -241,6 +248,11 @@ bool encode_tensor_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, const voi
 const CUtensorMap *cached_tensor_map_2d(CUtensorMapDataType dtype, const void *base, uint64_t inner, uint64_t outer,
                                         uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                                         CUtensorMapSwizzle swizzle);
+// A memoised 3D map: dims innermost first, byte strides of dims 1 and 2 (any
+// order; each a multiple of 16), box innermost first.
+const CUtensorMap *cached_tensor_map_3d(CUtensorMapDataType dtype, const void *base, uint64_t d0, uint64_t d1,
+                                        uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0,
+                                        uint32_t b1, uint32_t b2, CUtensorMapSwizzle swizzle);
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device, size).
 cudaError_t ensure_smem_attr(const void *kernel, int bytes);
 

@@ -130,12 +130,36 @@ def test_qmv_baseline_shapes(ctx, M, bits, N, K):
 
 
 def test_split_k_is_deterministic(ctx):
-    data = synthetic.quantized_linear(16, 4096, 14336, bits=4, seed=3)
+    # N = 16384 is past the warp-split plan (three 16-row tiles per SM), and
+    # so is K = 14336: blocks shared by several CTAs, combined across them.
+    data = synthetic.quantized_linear(16, 16384, 14336, bits=4, seed=3)
     bufs = _upload(ctx, data)
     y1, sel = _run_dense(ctx, data, bufs)
     assert sel.splits > 1
     y2, _ = _run_dense(ctx, data, bufs)
     assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("M,N,K,bits,rows", [(16, 4096, 4096, 4, 32), (16, 6144, 4096, 4, 48),
+                                              (16, 4096, 7168, 4, 32), (8, 1024, 4096, 8, 16),
+                                              (1, 4096, 2048, 4, 32), (13, 4008, 3584, 8, 32),
+                                              (5, 7000, 2048, 4, 48)])
+def test_qmv_warp_split_blocks(ctx, M, N, K, bits, rows):
+    """N up to three 16-row tiles per SM and K up to 32 stages (the
+    decoder's QKV and O shapes, the down projection's tensor-parallel shard)
+    takes the warp-split plan: one whole-K block per CTA, K split over the
+    CTA's warps and added in a fixed order (no combine across CTAs).  Every
+    row (including a partial last block) within 1e-5 of float64, and the same
+    bits twice."""
+    data = synthetic.quantized_linear(M, N, K, bits=bits, seed=23)
+    bufs = _upload(ctx, data)
+    y1, sel = _run_dense(ctx, data, bufs)
+    assert f"{rows}-row whole-K blocks" in sel.reason.decode(), sel.reason
+    assert sel.splits == 1
+    y2, _ = _run_dense(ctx, data, bufs)
+    assert torch.equal(y1, y2)
+    ref = _oracle_rows_f64(data, np.arange(N))
+    assert np.abs(y1.cpu().numpy() - ref).max() <= 1e-5 * max(1, np.abs(ref).max())
 
 
 @pytest.mark.parametrize("bits", [4, 8])

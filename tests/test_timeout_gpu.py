@@ -47,7 +47,7 @@ def combine_hook():
 
 def test_combine_timeout_is_reported_and_next_launch_is_correct(ctx):
     L = _lib.lib()
-    M, N, K = 4, 4096, 4096                 # split-K: blocks shared by several CTAs
+    M, N, K = 4, 16384, 4096                # split-K: blocks shared by several CTAs
     bufs = _operands(M, N, K, 4, ctx.device, seed=31)
     ptrs = [bufs[k].data_ptr() for k in ("x", "w", "s", "b")]
     d = dense_desc(M, N, K, 4)
@@ -75,7 +75,7 @@ def test_combine_timeout_is_reported_and_next_launch_is_correct(ctx):
 
 def test_noalloc_status_reports_a_timeout(ctx, combine_hook):
     L = _lib.lib()
-    M, N, K = 8, 4096, 4096
+    M, N, K = 8, 16384, 4096                # split-K: blocks shared by several CTAs
     bufs = _operands(M, N, K, 4, ctx.device, seed=32)
     ptrs = [bufs[k].data_ptr() for k in ("x", "w", "s", "b")]
     d = dense_desc(M, N, K, 4)
