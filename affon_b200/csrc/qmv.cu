@@ -305,28 +305,43 @@ __device__ __forceinline__ void publish_tile(const Params &p, int64_t tile, int 
 // Final values of one thread for one 16-row tile: rows n0+g and n0+g+8,
 // activation rows 2t, 2t+1 (+8 for the second MMA column tile).  Called by
 // all 32 lanes of the warp.
+// Residual-epilogue operands of one thread for one 16-row tile (finish_tile's
+// layout): pre[mt][h] = {h[m][n], h[m][n+8], gamma[n], gamma[n+8]} for
+// activation row m = 2t + 8mt + h and weight rows n = n0 + g, n0 + g + 8.
+template <int MT>
+__device__ __forceinline__ void load_resid_operands(const Params &p, int64_t n0, int g, int t, float (&pre)[MT][2][4]) {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int m = 2 * t + 8 * mt + h;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int64_t n = n0 + g + 8 * e;
+                const bool ok = m < p.M && n < p.N;
+                pre[mt][h][e] = ok ? p.f.h_out[m * p.f.ld_h_out + n] : 0.0f;
+                pre[mt][h][2 + e] = ok && p.f.next_x ? bf16_bits_to_f32(p.f.next_gamma[n]) : 0.0f;
+            }
+        }
+}
+
 template <int MT>
 __device__ __forceinline__ void finish_tile(const Params &p, const float (&v)[MT][4], int64_t n0, int g, int t,
-                                            const float *rs) {
+                                            const float *rs, const float (*pre_in)[2][4] = nullptr) {
     // The residual epilogue reads h and the next norm's weights: issue all of
     // this thread's loads before its first store (one round trip, not one per
-    // element).
+    // element), unless the caller fetched them earlier (pre_in).
     float pre[MT][2][4];
     const bool resid = p.f.epi == EPI_RESID;
-    if (resid) {
+    if (resid && pre_in) {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int m = 2 * t + 8 * mt + h;
+            for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int64_t n = n0 + g + 8 * e;
-                    const bool ok = m < p.M && n < p.N;
-                    pre[mt][h][e] = ok ? p.f.h_out[m * p.f.ld_h_out + n] : 0.0f;
-                    pre[mt][h][2 + e] = ok && p.f.next_x ? bf16_bits_to_f32(p.f.next_gamma[n]) : 0.0f;
-                }
-            }
+                for (int e = 0; e < 4; ++e) pre[mt][h][e] = pre_in[mt][h][e];
+    } else if (resid) {
+        load_resid_operands<MT>(p, n0, g, t, pre);
     }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -715,6 +730,49 @@ __device__ __forceinline__ void stage_group_sums(const char *xsb, float *xs, int
     }
 }
 
+// One warp's share of a stage's group sums in the warp-split kernel: groups
+// part, part + T, ... (the loads of all of them first, as above).
+template <int GPS, int MT, int X_BOX, int T>
+__device__ __forceinline__ void stage_group_sums_part(const char *xsb, float *xs, int g, int t, int part) {
+    const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};  // bf16 1.0 pairs
+    constexpr int NG = (GPS + T - 1) / T;
+    uint4 v[NG][MT][2];
+#pragma unroll
+    for (int i = 0; i < NG; ++i) {
+        const int G = part + i * T;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            const char *row = xsb + (G < GPS ? G : 0) * X_BOX + (g + 8 * mt) * 128;
+            v[i][mt][0] = *reinterpret_cast<const uint4 *>(row + (((2 * t) ^ g) << 4));
+            v[i][mt][1] = *reinterpret_cast<const uint4 *>(row + (((2 * t + 1) ^ g) << 4));
+        }
+    }
+    float cx[NG][MT][4];
+#pragma unroll
+    for (int i = 0; i < NG; ++i)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            cx[i][mt][0] = cx[i][mt][1] = cx[i][mt][2] = cx[i][mt][3] = 0.f;
+            mma_bf16_16816(cx[i][mt], ones, v[i][mt][0].x, v[i][mt][0].y, cx[i][mt]);
+            mma_bf16_16816(cx[i][mt], ones, v[i][mt][0].z, v[i][mt][0].w, cx[i][mt]);
+            mma_bf16_16816(cx[i][mt], ones, v[i][mt][1].x, v[i][mt][1].y, cx[i][mt]);
+            mma_bf16_16816(cx[i][mt], ones, v[i][mt][1].z, v[i][mt][1].w, cx[i][mt]);
+        }
+    if (g == 0) {
+#pragma unroll
+        for (int i = 0; i < NG; ++i) {
+            const int G = part + i * T;
+            if (G < GPS) {
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    xs[G * 16 + 8 * mt + 2 * t] = cx[i][mt][0];
+                    xs[G * 16 + 8 * mt + 2 * t + 1] = cx[i][mt][1];
+                }
+            }
+        }
+    }
+}
+
 template <int BITS, int MT, int NT, int CW>
 __global__ void __launch_bounds__(32 * (CW + 2), 1)
     qmv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
@@ -1046,10 +1104,12 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
 // Warp-split whole-K kernel (M <= 16, N up to three 16-row tiles per SM).
 // One block of T 16-row tiles per CTA, streamed over the whole K range once,
 // so no block is combined across CTAs: consumer warp (tile t, K lane k of
-// KW) takes stages k, k + KW, k + 2 KW, ... of tile t.  One sum warp forms
-// the group sums X_g of every stage, as in the stream-K kernel (same MMAs,
-// same order), into a small shared ring beside the stage ring, so the affine
-// per-group step is the stream-K kernel's.  The K lanes' accumulators meet in
+// KW) takes stages k, k + KW, k + 2 KW, ... of tile t.  The group sums X_g
+// of a stage (the stream-K kernel's all-ones MMAs, same order) are split
+// over the T warps of its K lane -- warp t forms groups t, t + T, ... into a
+// small shared ring beside the stage ring -- and the lane's warps meet on a
+// named barrier before using them, so the affine per-group step is the
+// stream-K kernel's.  The K lanes' accumulators meet in
 // shared memory and are added in lane order (results do not depend on
 // scheduling); the lane-0 warps apply the epilogue.  The ring depth is a
 // multiple of KW, so every ring slot serves the stages of one K lane only: a
@@ -1057,13 +1117,17 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
 // its parity wait never runs a phase ahead.  A stage is two TMA loads (the
 // packed rows; the activation columns of its groups as one 3D box), the
 // block's scales and biases one load each per launch: at these block heights
-// the TMA work per stage, not its bytes, sets the streaming rate.  The
-// producer warp forms the RMSNorm row scales after its first ring fill.
+// the TMA work per stage, not its bytes, sets the streaming rate.  The spare
+// warp fetches what the epilogue reads (the residual rows and next-norm
+// weights) into shared memory at the start, while the stages stream, and
+// forms the RMSNorm row scales.  A lane's group-sum slot is rewritten only
+// after its warps met on a later stage's barrier, so the ring depth is at
+// least 2 KW.
 template <int BITS, int MT, int T>
 struct WsShape {
     static constexpr int KW = T == 3 ? 3 : 10 / T;  // K lanes
     static constexpr int CW = T * KW;               // consumer warps
-    static constexpr int THREADS = 32 * (CW + 2);   // consumers, producer, sum warp
+    static constexpr int THREADS = 32 * (CW + 2);   // consumers, producer, spare warp
     static constexpr int ROWS = 16 * T;
     static constexpr int XR = 16;
     static constexpr int X_BOX = XR * 128;
@@ -1144,12 +1208,13 @@ __global__ void __launch_bounds__(WsShape<BITS, MT, T>::THREADS, 1)
     char *ring = smem;
     char *slab = ring + S * Sh::BYTES;  // scales [ROWS][SP], then biases [ROWS][SP]
     float *red = reinterpret_cast<float *>(slab + ws_slab_bytes(ROWS, p.K));
-    float *xsums = red + Sh::RED / 4;  // [slot][group][16 activation rows]
-    uint64_t *full = reinterpret_cast<uint64_t *>(xsums + MAX_WS_STAGES * GPS * 16);
+    float *xsums = red + Sh::RED / 4;               // [slot][group][16 activation rows]
+    float *hg = xsums + MAX_WS_STAGES * GPS * 16;    // residual operands [tile][mt][h][4][lane]
+    uint64_t *full = reinterpret_cast<uint64_t *>(hg + T * MT * 8 * 32);
     uint64_t *empty = full + MAX_WS_STAGES;
-    uint64_t *xsfull = empty + MAX_WS_STAGES;
-    uint64_t *sbfull = xsfull + MAX_WS_STAGES;
-    volatile int *abort = reinterpret_cast<volatile int *>(sbfull + 1);
+    uint64_t *sbfull = empty + MAX_WS_STAGES;
+    uint64_t *hgbar = sbfull + 1;
+    volatile int *abort = reinterpret_cast<volatile int *>(hgbar + 1);
     __shared__ float s_rscale[MAX_XR];  // RMSNorm row scales (row_scale mode)
     __shared__ uint64_t s_rsbar;        // completes once s_rscale holds them
     const float *rs = p.f.row_ss ? s_rscale : nullptr;
@@ -1159,10 +1224,10 @@ __global__ void __launch_bounds__(WsShape<BITS, MT, T>::THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], T + 1);  // the T warps of the slot's K lane and the sum warp
-            mbar_init(&xsfull[s], 1);
+            mbar_init(&empty[s], T);  // the T warps of the slot's K lane
         }
         mbar_init(sbfull, 1);
+        mbar_init(hgbar, 1);
         mbar_init(&s_rsbar, 1);
         *abort = 0;
         fence_mbar_init();
@@ -1196,13 +1261,6 @@ __global__ void __launch_bounds__(WsShape<BITS, MT, T>::THREADS, 1)
             pdl_wait();
             for (int j = 0; j < pre; ++j) load_x(j, j);
         }
-        // The row scales (all lanes), while the first ring fill lands and is
-        // consumed: no refill is due before the first stage is released.
-        __syncwarp();
-        if (rs) {
-            pdl_wait();
-            ws_row_scales<MT>(p, lane, s_rscale, &s_rsbar);
-        }
         if (lane == 0) {
             uint32_t issued_mask = pre >= 32 ? ~0u : (1u << pre) - 1u, issued_par = 0;
             for (int j = pre; j < spb; ++j) {
@@ -1220,22 +1278,23 @@ __global__ void __launch_bounds__(WsShape<BITS, MT, T>::THREADS, 1)
             mbar_wait_drain(sbfull, 0);
         }
         __syncwarp();
-    } else if (warp == CW + 1) {  // ----------------------------- group sums
-        // X_g = sum_{k in g} x[m][k] for every activation row and stage
-        // (stage_group_sums).
-        for (int j = 0; j < spb; ++j) {
-            const int slot = j % S;
-            const uint32_t ph = static_cast<uint32_t>(j / S) & 1u;
-            mbar_wait(&full[slot], ph, abort, p.status);
-            stage_group_sums<GPS, MT, Sh::X_BOX, 16, GPS>(ring + slot * Sh::BYTES + Sh::W, xsums + slot * GPS * 16, g,
-                                                          t);
-            fence_proxy_async_smem();  // x reads before the slot's next TMA fill
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&xsfull[slot]);
-                mbar_arrive(&empty[slot]);
+    } else if (warp == CW + 1) {  // --------- epilogue operands, row scales
+        pdl_wait();
+        if (p.f.epi == EPI_RESID) {
+            for (int tl = 0; tl < T; ++tl) {
+                float pre[MT][2][4];
+                load_resid_operands<MT>(p, static_cast<int64_t>(blk) * ROWS + tl * 16, g, t, pre);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) hg[(((tl * MT + mt) * 2 + h) * 4 + e) * 32 + lane] = pre[mt][h][e];
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(hgbar);
         }
+        if (rs) ws_row_scales<MT>(p, lane, s_rscale, &s_rsbar);
     } else {  // ------------------------------------------------- consumers
         pdl_wait();
         const int tile = warp % T, kl = warp / T;
@@ -1250,7 +1309,7 @@ __global__ void __launch_bounds__(WsShape<BITS, MT, T>::THREADS, 1)
             mbar_wait(&full[slot], ph, abort, p.status);
             const char *sw = ring + slot * Sh::BYTES;
             const char *xsb = sw + Sh::W;
-            const float *xs = xsums + slot * GPS * 16;
+            float *xs = xsums + slot * GPS * 16;
             uint32_t sv[2][GPS / 2], bv[2][GPS / 2];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -1264,7 +1323,10 @@ __global__ void __launch_bounds__(WsShape<BITS, MT, T>::THREADS, 1)
                     bv[h][0] = *reinterpret_cast<const uint32_t *>(bsl + off);
                 }
             }
-            mbar_wait(&xsfull[slot], ph, abort, p.status);
+            // This warp's share of the stage's group sums, then the K lane's
+            // warps meet (named barrier 2 + k).
+            stage_group_sums_part<GPS, MT, Sh::X_BOX, T>(xsb, xs, g, t, tile);
+            if constexpr (T > 1) named_bar_sync(2 + kl, T * 32);
 #pragma unroll
             for (int G = 0; G < GPS; ++G) {
                 uint32_t xf[MT][8];
@@ -1367,7 +1429,20 @@ __global__ void __launch_bounds__(WsShape<BITS, MT, T>::THREADS, 1)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) accf[mt][i] += red[(((k * T + tile) * MT + mt) * 4 + i) * 32 + lane];
             if (rs) mbar_wait(&s_rsbar, 0, abort, p.status);  // the row scales are out
-            finish_tile<MT>(p, accf, static_cast<int64_t>(blk) * ROWS + tile * 16, g, t, rs);
+            const int64_t n0 = static_cast<int64_t>(blk) * ROWS + tile * 16;
+            if (p.f.epi == EPI_RESID) {
+                mbar_wait(hgbar, 0, abort, p.status);
+                float pre[MT][2][4];
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) pre[mt][h][e] = hg[(((tile * MT + mt) * 2 + h) * 4 + e) * 32 + lane];
+                finish_tile<MT>(p, accf, n0, g, t, rs, pre);
+            } else {
+                finish_tile<MT>(p, accf, n0, g, t, rs);
+            }
         }
         if (p.f.epi == EPI_RESID_AR) {
             ar_signal<CW>(p, blk * p.max_slots, tid);
@@ -1590,13 +1665,13 @@ static QmvPlan ws_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     const int rows = 16 * T;
     if (qmv::ws_slab_pitch(static_cast<int>(a.K)) > 256) return p;  // one TMA box per slab
     // alignment slack, scale/bias slabs, K-lane sums, group-sum ring
-    // (4 groups x 16 rows per slot at most), full/empty/xsfull barriers and
-    // the slab barrier, the abort word
+    // (4 groups x 16 rows per slot at most), residual operands (2 KiB per
+    // tile), full/empty barriers, the slab and operand barriers, the abort word
     const int overhead = 1024 + qmv::ws_slab_bytes(rows, static_cast<int>(a.K)) + red +
-                         qmv::MAX_WS_STAGES * 4 * 16 * 4 + (3 * qmv::MAX_WS_STAGES + 1) * 8 + 64;
+                         qmv::MAX_WS_STAGES * 4 * 16 * 4 + T * 2048 + (2 * qmv::MAX_WS_STAGES + 2) * 8 + 64;
     int stages = std::min(qmv::MAX_WS_STAGES, (kSmemCap - overhead) / bytes);
-    stages -= stages % kw;  // every ring slot serves one K lane
-    if (stages < kw) return p;
+    stages -= stages % kw;   // every ring slot serves one K lane
+    if (stages < 2 * kw) return p;  // group-sum slots are reused only after a later stage's barrier
     const int64_t nblocks = (a.N + rows - 1) / rows;
     const size_t need = kPartialOffset + static_cast<size_t>(nblocks) * a.M * rows * 4 + qmv_prep_bytes(a);
     if (need > workspace_bytes) return p;
