@@ -7,7 +7,8 @@
 // block-row x 128-byte stage of the packed weight matrix through a ring of
 // shared-memory stages with 2D TMA loads (128-byte swizzle), together with the
 // matching boxes of bf16 scales and biases (8 groups wide) and the stage's
-// activation columns (16 or 32 rows x 64 columns per group, 128-byte swizzle).
+// activation columns (16 or 32 rows x 64 columns per group, 128-byte swizzle;
+// one 3D box per stage).
 // The ring holds ~190 KB per SM in flight without costing registers, and the
 // activations need no separate staging pass.  Twelve consumer warps decode the
 // packed words in registers and feed tensor cores: for M <= 16 each warp owns
@@ -834,11 +835,9 @@ __global__ void __launch_bounds__(32 * (CW + 2), 1)
                                      stream_policy);
                 }
             };
-            auto load_x = [&](int stage, int64_t i) {
+            auto load_x = [&](int stage, int64_t i) {  // box: 64 columns x XR rows x GPS groups
                 const int blk = static_cast<int>(i / p.spb), st = static_cast<int>(i - int64_t(blk) * p.spb);
-                char *dst = ring + stage * Sh::BYTES + Sh::W + 2 * Sh::SB;
-#pragma unroll
-                for (int G = 0; G < GPS; ++G) tma_load_2d(dst + G * Sh::X_BOX, &xmap, &full[stage], st * KPS + G * GROUP, 0);
+                tma_load_3d(ring + stage * Sh::BYTES + Sh::W + 2 * Sh::SB, &xmap, &full[stage], 0, 0, st * GPS);
             };
             // First pass over the ring: weights, scales and biases need nothing
             // from the preceding kernel; the activations do.
@@ -1892,8 +1891,8 @@ cudaError_t launch_qmv(const QmmArgs &a, const QmvPlan &plan, void *workspace, c
                                     box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
         !(bm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b.ptr, a.K / 64, a.N, a.b.row_stride * 2, 8,
                                     box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-        !(xm = cached_tensor_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xq, a.K, a.M, ldxq * 2, 64, xr,
-                                    CU_TENSOR_MAP_SWIZZLE_128B)))
+        !(xm = cached_tensor_map_3d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xq, 64, a.M, a.K / 64, ldxq * 2, 128, 64, xr,
+                                    a.bits == 4 ? 4 : 2, CU_TENSOR_MAP_SWIZZLE_128B)))
         return cudaErrorInvalidValue;
     const bool b4 = a.bits == 4;
     switch (plan.variant) {
