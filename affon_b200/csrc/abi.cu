@@ -521,7 +521,8 @@ int affon_b200_qmv_fused(affon_b200_ctx *ctx, const affon_b200_qmm_desc *desc, c
     afb::QmmArgs a = make_args(desc, x, w, s, b, y ? y : fake);
     const char *why = "";
     if (!afb::qmv_supported(a, &why)) return fail(AFFON_B200_UNSUPPORTED, "qmv_fused: %s", why);
-    const afb::QmvPlan plan = afb::qmv_plan(a, ctx->num_sms, ctx->workspace_bytes);
+    // The fused tensor-parallel exchange (epilogue 4) runs on the stream-K plan.
+    const afb::QmvPlan plan = afb::qmv_plan(a, ctx->num_sms, ctx->workspace_bytes, f.epi != 4);
     if (plan.splits < 1) return fail(AFFON_B200_UNSUPPORTED, "qmv_fused: no plan fits the context workspace");
     if (f.epi == 4) {
         const int64_t units = (a.N + plan.rows - 1) / plan.rows * plan.max_slots;

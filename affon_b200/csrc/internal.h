@@ -98,7 +98,9 @@ struct QmvFusion {
     unsigned *tp_flags_local = nullptr;
 };
 bool qmv_supported(const QmmArgs &a, const char **why);
-QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes);
+// allow_ws = false keeps to the stream-K kernel (the tensor-parallel fused
+// exchange, whose multi-GPU runs cover that kernel).
+QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes, bool allow_ws = true);
 size_t qmv_workspace_bytes(const QmmArgs &a, const QmvPlan &p);
 // Bytes at the end of the qmv workspace that hold pair-ordered x (4-bit, x_mode 0).
 size_t qmv_prep_bytes(const QmmArgs &a);

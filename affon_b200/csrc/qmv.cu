@@ -1685,8 +1685,8 @@ static QmvPlan ws_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
     return p;
 }
 
-QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes) {
-    {
+QmvPlan qmv_plan(const QmmArgs &a, int num_sms, size_t workspace_bytes, bool allow_ws) {
+    if (allow_ws) {
         const QmvPlan w = ws_plan(a, num_sms, workspace_bytes);
         if (w.splits) return w;
     }
