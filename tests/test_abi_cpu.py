@@ -169,3 +169,24 @@ def test_prefill_selection_by_rows_and_policy():
     d = dense_desc(512, 4096, 4096, 4)
     d.numerical_policy = _lib.POLICY["exact_only"]
     assert L.affon_b200_select(d, _lib.Selection()) != 0
+
+
+def test_qmv_plan_by_shape():
+    """Decode plans (148 SMs): N up to three 16-row tiles per SM with K up to 32
+    stages takes whole-K blocks split over a CTA's warps (no cross-CTA
+    combine: one K segment per tile); longer K, larger N and M > 16 stream K
+    across CTAs and combine."""
+    L = _lib.lib()
+    cases = [((16, 4096, 4096, 4), "32-row whole-K blocks over 128 CTAs"),    # O
+             ((16, 6144, 4096, 4), "48-row whole-K blocks over 128 CTAs"),    # QKV
+             ((8, 1024, 4096, 8), "16-row whole-K blocks over 64 CTAs"),
+             ((16, 4096, 7168, 4), "32-row whole-K blocks"),                  # down shard at TP2
+             ((16, 4096, 14336, 4), "stream-K"),                             # down: 56 stages
+             ((32, 4096, 4096, 4), "stream-K"),                              # M > 16
+             ((16, 16384, 4096, 4), "stream-K")]                             # 7 tiles per SM
+    for (M, N, K, bits), want in cases:
+        sel = _lib.Selection()
+        assert L.affon_b200_select(dense_desc(M, N, K, bits), sel) == 0, _lib.last_error()
+        reason = sel.reason.decode()
+        assert want in reason, (M, N, K, reason)
+        assert (sel.splits == 1) == ("whole-K" in want), (M, N, K, sel.splits, reason)
